@@ -1,0 +1,122 @@
+/* leafq -- B200 (sm_100a) quantised-linear operators behind a plain C ABI.
+ *
+ * Drop-in boundary for Leaf's quantised Linear: every entry point takes
+ * device pointers, plain sizes and a cudaStream_t (passed as void*), returns
+ * an int status, allocates nothing on the hot path and never throws.  All
+ * calls are stream-ordered and asynchronous; results are ready when the
+ * stream is.  Calls on different streams may run concurrently (the library
+ * keeps no mutable per-call host state besides the thread-local error text).
+ *
+ * Layouts are the reference's:
+ *   x       fp32 [tokens, cols] token-major (Decoder::Impl::linear input)
+ *   weight  row-major [rows, cols]; bits 8: one int8 per value; bits 4: two
+ *           signed nibbles per byte, low nibble = even column
+ *           (decoder.cpp:236-251, tools/export_decoder.py:91-105); bits 32:
+ *           fp32.  16-byte aligned base for the fast paths.
+ *   scales  fp32 [rows, cols / group] (group == cols for per-row INT8)
+ *   bias    fp32 [rows] or NULL
+ *   y       fp32 [tokens, rows] token-major (decoder.cpp:1229)
+ *
+ * Status codes: LEAFQ_OK on success; anything else leaves the outputs
+ * unspecified and leafq_last_error() describes the failure.
+ */
+#ifndef LEAFQ_H
+#define LEAFQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LEAFQ_OK 0
+#define LEAFQ_ERR_INVALID 1     /* bad argument: null pointer, shape, alignment */
+#define LEAFQ_ERR_CUDA 2        /* a CUDA runtime call failed */
+#define LEAFQ_ERR_UNSUPPORTED 3 /* valid for the reference, not built here */
+#define LEAFQ_ERR_TIMEOUT 4     /* a bounded device-side wait gave up */
+#define LEAFQ_ERR_NONFINITE 5   /* graph quantiser saw a non-finite value */
+
+/* flags */
+/* Accumulate per-group partial sums with two roundings, as the reference's
+ * AVX-VNNI prefill tile does (decoder.cpp:695-700), instead of the fused
+ * multiply-add of its AVX2 kernels (decoder.cpp:567, 614).  Only matters
+ * with several groups per row. */
+#define LEAFQ_FLAG_VNNI_ROUNDING 0x1u
+/* Launch with programmatic dependent launch: the kernel may start, and
+ * begin streaming weights, scales and bias, before the previous kernel in
+ * the stream has finished; it still waits for that kernel before reading x
+ * or writing y.  Only valid when the previous kernel does not write this
+ * call's weights, scales or bias (true inside a decode step, where they are
+ * read-only). */
+#define LEAFQ_FLAG_PDL 0x2u
+
+/* Human-readable description of this thread's last failure ("" if none). */
+const char* leafq_last_error(void);
+
+/* ABI version of this library (major * 100 + minor). */
+int leafq_version(void);
+
+/* Reads and clears the device error word that bounded waits set when they
+ * give up.  Synchronises the current device.  LEAFQ_OK or LEAFQ_ERR_TIMEOUT. */
+int leafq_device_status(void);
+
+/* Per-token dynamic activation quantisation.
+ * Replaces decoder.cpp:1028-1044 (scale = max(absmax / 127, 1e-12), codes =
+ * round-half-even(x * (1 / scale)) as quantize_input_avx, :618-627).  q is
+ * int8 [tokens, cols] (the reference's int16 container holds the same values
+ * in [-127, 127]; its VNNI uint8 container holds q + 128), scales fp32
+ * [tokens]. */
+int leafq_quantize_act(void* stream, const float* x, int64_t tokens, int64_t cols, int8_t* q,
+                       float* scales);
+
+/* Bytes of caller-provided device workspace leafq_linear needs for this
+ * shape (0 when the call needs none).  The workspace must be 256-byte
+ * aligned. */
+size_t leafq_linear_workspace_bytes(int64_t tokens, int64_t cols, int bits, int64_t group,
+                                    int activation_bits);
+
+/* The quantised Linear: Decoder::Impl::linear(input, tokens, name, output)
+ * for one named weight (decoder.cpp:994-1233).
+ *   activation_bits 8  + bits 8/4: W8A8 / W4A8 -- per-token dynamic int8
+ *       activations, exact int32 group sums, then per group in order
+ *       result = fma(float(acc) * sx, sw, result), plus bias.
+ *   activation_bits 32 + bits 4/8/32: weight-only, fp32 activations, in the
+ *       summation order of dot_avx (decoder.cpp:355-391).
+ * workspace may be NULL when leafq_linear_workspace_bytes() returned 0. */
+int leafq_linear(void* stream, const float* x, int64_t tokens, int64_t cols, const void* weight,
+                 const float* weight_scales, int64_t rows, int bits, int64_t group,
+                 int activation_bits, const float* bias, float* y, void* workspace,
+                 size_t workspace_bytes, uint32_t flags);
+
+/* Integer linear from codes already produced by leafq_quantize_act (or by
+ * the reference's quantiser).  acc, when not NULL, receives every int32
+ * group sum, layout [tokens, rows, cols / group]: the accumulator the
+ * reference keeps in quant_dot_avx / quant_vnni_tile (decoder.cpp:536-570,
+ * 661-702), exposed for bit-exact checking. */
+int leafq_linear_int_q(void* stream, const int8_t* q, const float* scales, int64_t tokens,
+                       int64_t cols, const void* weight, const float* weight_scales, int64_t rows,
+                       int bits, int64_t group, const float* bias, float* y, int32_t* acc,
+                       uint32_t flags);
+
+/* Graph executor static INT8 activation quantiser (executor.cpp:220-230):
+ * q = nearbyint(clamp(x / scale, -127, 127)).  The reference throws on a
+ * non-finite value; here the kernel sets *error_flag (device int32, caller
+ * clears it) to 1, and the call itself returns LEAFQ_ERR_INVALID for a
+ * non-finite or non-positive scale. */
+int leafq_graph_quantize(void* stream, const float* x, int64_t count, float scale, int8_t* q,
+                         int32_t* error_flag);
+
+/* Graph executor INT8 GEMM, leaf::kernels::gemm_i8_per_channel
+ * (engine/include/leaf/kernels/gemm.h:24-28, kernels/gemm.cpp:99-166):
+ * a int8 [m, k], b int8 [k, n] (n contiguous), out fp32 [m, n] =
+ * (float(a . b) * input_scale) * weight_scales[n] (+ bias[n]), then ReLU
+ * when activation == 1. */
+int leafq_gemm_i8_per_channel(void* stream, const int8_t* a, const int8_t* b, const float* bias,
+                              float input_scale, const float* weight_scales, float* out,
+                              int64_t m, int64_t k, int64_t n, int activation);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LEAFQ_H */

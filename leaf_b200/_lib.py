@@ -1,0 +1,83 @@
+"""ctypes binding of libleafq.so (the C ABI declared in include/leafq.h).
+
+The library must be present and loadable: there is no CPU or PyTorch
+fallback for any leafq operation.  A missing library raises immediately.
+"""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+PACKAGE = Path(__file__).resolve().parent
+LIBRARY = PACKAGE / "libleafq.so"
+HEADER = PACKAGE.parent / "include" / "leafq.h"
+
+LEAFQ_OK = 0
+LEAFQ_ERR_INVALID = 1
+LEAFQ_ERR_CUDA = 2
+LEAFQ_ERR_UNSUPPORTED = 3
+LEAFQ_ERR_TIMEOUT = 4
+LEAFQ_ERR_NONFINITE = 5
+
+LEAFQ_FLAG_VNNI_ROUNDING = 0x1
+LEAFQ_FLAG_PDL = 0x2
+
+_vp = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_int = ctypes.c_int
+_u32 = ctypes.c_uint32
+_f32 = ctypes.c_float
+_size = ctypes.c_size_t
+
+_SIGNATURES = {
+    "leafq_last_error": ([], ctypes.c_char_p),
+    "leafq_version": ([], _int),
+    "leafq_device_status": ([], _int),
+    "leafq_quantize_act": ([_vp, _vp, _i64, _i64, _vp, _vp], _int),
+    "leafq_linear_workspace_bytes": ([_i64, _i64, _int, _i64, _int], _size),
+    "leafq_linear": ([_vp, _vp, _i64, _i64, _vp, _vp, _i64, _int, _i64, _int, _vp, _vp, _vp, _size,
+                      _u32], _int),
+    "leafq_linear_int_q": ([_vp, _vp, _vp, _i64, _i64, _vp, _vp, _i64, _int, _i64, _vp, _vp, _vp,
+                            _u32], _int),
+    "leafq_graph_quantize": ([_vp, _vp, _i64, _f32, _vp, _vp], _int),
+    "leafq_gemm_i8_per_channel": ([_vp, _vp, _vp, _vp, _f32, _vp, _vp, _i64, _i64, _i64, _int],
+                                  _int),
+}
+
+_lib = None
+
+
+class LeafError(RuntimeError):
+    """A leafq call failed; mirrors the reference's std::runtime_error."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(f"Leaf decoder: {message} (leafq status {status})")
+        self.status = status
+
+
+def declared_symbols() -> list[str]:
+    """Every function name include/leafq.h declares."""
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"\b(leafq_[a-z0-9_]+)\s*\(", text)))
+
+
+def load() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not LIBRARY.exists():
+            raise LeafError(LEAFQ_ERR_UNSUPPORTED,
+                            f"{LIBRARY} is missing; build it with `python -m leaf_b200.build`")
+        lib = ctypes.CDLL(str(LIBRARY))
+        for name, (args, restype) in _SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.argtypes = args
+            fn.restype = restype
+        _lib = lib
+    return _lib
+
+
+def check(status: int) -> None:
+    if status != LEAFQ_OK:
+        message = load().leafq_last_error().decode(errors="replace")
+        raise LeafError(status, message or "unknown failure")

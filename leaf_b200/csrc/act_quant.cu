@@ -1,0 +1,117 @@
+// Activation quantisers.
+//
+// quantize_act_kernel: per-token dynamic INT8 (decoder.cpp:1028-1038 with
+//   quantize_input_avx, :618-627).  One 256-thread block per token row: a
+//   block-wide absmax (fmaxf is exact and order-free), then
+//   scale = max(absmax / 127, 1e-12) with IEEE division, multiplier =
+//   1 / scale (IEEE), code = round-half-even(x * multiplier).  __fmul_rn and
+//   __fdiv_rn keep the compiler from fusing or approximating any step.
+// graph_quantize_kernel: the graph executor's static quantiser
+//   (executor.cpp:220-230): division by the calibrated scale, clamp to
+//   [-127, 127], nearbyint.
+#include "leafq_device.cuh"
+#include "leafq_internal.h"
+
+namespace leafq {
+namespace {
+
+constexpr int kQuantThreads = 256;
+
+__device__ __forceinline__ int8_t code_of(float value, float multiplier) {
+    int r = __float2int_rn(__fmul_rn(value, multiplier));
+    r = r > 127 ? 127 : (r < -128 ? -128 : r);
+    return static_cast<int8_t>(r);
+}
+
+__device__ __forceinline__ float block_max(float v, float* scratch) {
+    for (int offset = 16; offset > 0; offset >>= 1)
+        v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, offset));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) scratch[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+        v = lane < (blockDim.x >> 5) ? scratch[lane] : 0.0f;
+        for (int offset = 16; offset > 0; offset >>= 1)
+            v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, offset));
+        if (lane == 0) scratch[32] = v;
+    }
+    __syncthreads();
+    return scratch[32];
+}
+
+__global__ void __launch_bounds__(kQuantThreads) quantize_act_kernel(const float* __restrict__ x,
+                                                                      int64_t cols,
+                                                                      int8_t* __restrict__ q,
+                                                                      float* __restrict__ scales) {
+    __shared__ float scratch[33];
+    grid_dependency_wait();
+    grid_launch_dependents();
+    const int64_t row = blockIdx.x;
+    const float* in = x + row * cols;
+    int8_t* out = q + row * cols;
+    const bool vec = (cols % 4 == 0) && ((reinterpret_cast<uintptr_t>(in) & 15u) == 0);
+    float m = 0.0f;
+    if (vec) {
+        const float4* in4 = reinterpret_cast<const float4*>(in);
+        for (int64_t i = threadIdx.x; i < cols / 4; i += blockDim.x) {
+            const float4 v = __ldg(in4 + i);
+            m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        }
+    } else {
+        for (int64_t i = threadIdx.x; i < cols; i += blockDim.x) m = fmaxf(m, fabsf(__ldg(in + i)));
+    }
+    const float absmax = block_max(m, scratch);
+    const float scale = fmaxf(__fdiv_rn(absmax, 127.0f), 1e-12f);
+    const float multiplier = __fdiv_rn(1.0f, scale);
+    if (threadIdx.x == 0) scales[row] = scale;
+    if (vec && ((reinterpret_cast<uintptr_t>(out) & 3u) == 0)) {
+        const float4* in4 = reinterpret_cast<const float4*>(in);
+        char4* out4 = reinterpret_cast<char4*>(out);
+        for (int64_t i = threadIdx.x; i < cols / 4; i += blockDim.x) {
+            const float4 v = __ldg(in4 + i);
+            out4[i] = make_char4(code_of(v.x, multiplier), code_of(v.y, multiplier),
+                                 code_of(v.z, multiplier), code_of(v.w, multiplier));
+        }
+    } else {
+        for (int64_t i = threadIdx.x; i < cols; i += blockDim.x)
+            out[i] = code_of(__ldg(in + i), multiplier);
+    }
+}
+
+__global__ void graph_quantize_kernel(const float* __restrict__ x, int64_t count, float scale,
+                                      int8_t* __restrict__ q, int32_t* error_flag) {
+    grid_dependency_wait();
+    grid_launch_dependents();
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const float v = x[i];
+        if (!isfinite(v)) {
+            if (error_flag) atomicExch(error_flag, 1);
+            q[i] = 0;
+            continue;
+        }
+        float scaled = __fdiv_rn(v, scale);
+        scaled = fmaxf(-127.0f, fminf(127.0f, scaled));
+        q[i] = static_cast<int8_t>(__float2int_rn(scaled));
+    }
+}
+
+}  // namespace
+
+int launch_quantize_act(cudaStream_t s, const float* x, int64_t tokens, int64_t cols, int8_t* q,
+                        float* scales, bool pdl) {
+    if (tokens == 0) return LEAFQ_OK;
+    return launch(quantize_act_kernel, dim3(static_cast<unsigned>(tokens)), dim3(kQuantThreads), 0,
+                  s, pdl, "quantize_act", x, cols, q, scales);
+}
+
+int launch_graph_quantize(cudaStream_t s, const float* x, int64_t count, float scale, int8_t* q,
+                          int32_t* error_flag) {
+    if (count == 0) return LEAFQ_OK;
+    const int64_t blocks64 = (count + 255) / 256;
+    const unsigned blocks = static_cast<unsigned>(blocks64 < 4 * 148 * 8 ? blocks64 : 4 * 148 * 8);
+    return launch(graph_quantize_kernel, dim3(blocks), dim3(256), 0, s, false, "graph_quantize", x,
+                  count, scale, q, error_flag);
+}
+
+}  // namespace leafq

@@ -1,0 +1,290 @@
+// W8A8 prefill GEMM on the 5th-generation tensor cores (tcgen05.mma
+// kind::i8, int32 accumulators in tensor memory).
+//
+// Replaces the prefill branch of Decoder::Impl::linear for per-row INT8
+// weights: the VNNI 2x4 tile (decoder.cpp:661-702) or the AVX2 4x2 tile
+// (:571-617) over all rows, with the per-token codes produced beforehand by
+// quantize_act_kernel.  Both CPU tiles and this kernel produce the exact
+// int32 dot product of every (token, row), and the same epilogue:
+//   y = fma(float(acc) * sx[token], sw[row], 0.0f) + (bias[row] or 0.0f).
+//
+// Tiling: D[128 tokens, 256 rows] per tile (one UMMA of M=128, N=256, K=32
+// per instruction, four per 128-byte K block).  Operands are K-major: the
+// codes [tokens, cols] and the weights [rows, cols] are both row-major with
+// K contiguous, loaded by TMA with 128-byte swizzle into a 4-stage ring
+// (48 KB per stage).  Warp roles (192 threads, persistent over tiles):
+//   warp 0: TMA producer (one elected lane), no multicast;
+//   warp 1: allocates 512 TMEM columns (two 256-column accumulators so the
+//           epilogue of one tile overlaps the MMAs of the next) and issues
+//           the MMAs from one elected lane;
+//   warps 2-5: epilogue, each reading its 32 TMEM lanes (= tokens) with
+//           tcgen05.ld and writing 32 consecutive fp32 outputs per load.
+// Every mbarrier wait is bounded; on a timeout the roles stop, the TMEM is
+// freed and the kernel returns with the device error word set.
+#include <mutex>
+#include <unordered_map>
+
+#include "leafq_device.cuh"
+#include "leafq_internal.h"
+
+namespace leafq {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 128;  // bytes (= int8 elements) of K per stage
+constexpr int UMMA_K = 32;
+constexpr int kStages = 4;
+constexpr int kThreads = 192;
+constexpr int kAccCols = BN;      // TMEM columns per accumulator
+constexpr int kTmemCols = 2 * kAccCols;
+constexpr int kABytes = BM * BK;  // 16 KB
+constexpr int kBBytes = BN * BK;  // 32 KB
+constexpr size_t kSmemBytes = (size_t)kStages * (kABytes + kBBytes) + 1024 /*barriers*/ + 1024 /*align*/;
+
+struct GemmArgs {
+    const float* sx;
+    const float* ws;
+    const float* bias;
+    float* y;
+    int64_t tokens;
+    int64_t rows;
+    int64_t cols;
+    int m_tiles;
+    int n_tiles;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_w8a8_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_w,
+                    const GemmArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    // 1024-byte alignment for the swizzled operand tiles.
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    uint8_t* a_tiles = smem;
+    uint8_t* b_tiles = smem + (size_t)kStages * kABytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(b_tiles + (size_t)kStages * kBBytes);
+    uint64_t* empty = full + kStages;
+    uint64_t* acc_full = empty + kStages;
+    uint64_t* acc_empty = acc_full + 2;
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int kblocks = static_cast<int>((a.cols + BK - 1) / BK);
+    const int tiles = a.m_tiles * a.n_tiles;
+
+    if (warp == 0 && lane == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&acc_full[i], 1);
+            mbar_init(&acc_empty[i], 4);  // one arrival per epilogue warp
+        }
+        fence_barrier_init();
+        prefetch_tensormap(&map_q);
+        prefetch_tensormap(&map_w);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_holder, kTmemCols);
+        tmem_relinquish();
+    }
+    tcgen05_fence_before();
+    __syncthreads();
+    tcgen05_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+    grid_launch_dependents();
+
+    if (warp == 0) {
+        // ------------------------------------------------ TMA producer
+        if (elect_one_sync()) {
+            const uint64_t keep = l2_policy_evict_last();
+            grid_dependency_wait();  // the codes come from the previous kernel
+            int it = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+                const int m0 = (tile % a.m_tiles) * BM;
+                const int n0 = (tile / a.m_tiles) * BN;
+                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                    const int s = it % kStages;
+                    if (it >= kStages && !mbar_wait(&empty[s], ((it / kStages) - 1) & 1, kSiteGemmEmpty)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full[s], kABytes + kBBytes);
+                    tma_load_2d(a_tiles + (size_t)s * kABytes, &map_q, kb * BK, m0, &full[s], keep);
+                    tma_load_2d(b_tiles + (size_t)s * kBBytes, &map_w, kb * BK, n0, &full[s], keep);
+                }
+            }
+            // Drain: the last use of every stage must have landed before the
+            // block can exit (normally already true).
+            for (int back = 0; back < kStages && back < it; ++back) {
+                const int i = it - 1 - back;
+                mbar_wait(&full[i % kStages], (i / kStages) & 1, kSiteGemmFull);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer
+        if (elect_one_sync()) {
+            const uint32_t idesc = umma_idesc_i8(BM, BN);
+            int it = 0, local = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++local) {
+                const int acc = local & 1;
+                if (local >= 2 && !mbar_wait(&acc_empty[acc], ((local >> 1) - 1) & 1, kSiteGemmAccEmpty)) break;
+                tcgen05_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * kAccCols;
+                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                    const int s = it % kStages;
+                    if (!mbar_wait(&full[s], (it / kStages) & 1, kSiteGemmFull)) {
+                        ok = false;
+                        break;
+                    }
+                    tcgen05_fence_after();
+                    const uint64_t adesc = umma_desc_k_sw128(smem_u32(a_tiles + (size_t)s * kABytes));
+                    const uint64_t bdesc = umma_desc_k_sw128(smem_u32(b_tiles + (size_t)s * kBBytes));
+#pragma unroll
+                    for (int k = 0; k < BK / UMMA_K; ++k) {
+                        // Advance the start address by k * 32 bytes (>> 4).
+                        umma_i8(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
+                    }
+                    umma_commit(&empty[s]);
+                }
+                if (ok) umma_commit(&acc_full[acc]);
+            }
+        }
+    } else {
+        // ------------------------------------------------ epilogue (warps 2-5)
+        grid_dependency_wait();
+        const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
+        int local = 0;
+        for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
+            const int acc = local & 1;
+            const int m0 = (tile % a.m_tiles) * BM;
+            const int n0 = (tile / a.m_tiles) * BN;
+            if (!mbar_wait(&acc_full[acc], (local >> 1) & 1, kSiteGemmAccFull)) break;
+            tcgen05_fence_after();
+            const int64_t m = m0 + quarter * 32 + lane;
+            const bool row_live = m < a.tokens;
+            const float token_scale = row_live ? __ldg(a.sx + m) : 0.0f;
+            float* out = a.y + m * a.rows;
+            const bool vec = (a.rows % 4) == 0;
+            for (int c = 0; c < BN; c += 32) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(tmem_base + acc * kAccCols + c + ((uint32_t)(quarter * 32) << 16), r);
+                tmem_wait_ld();
+                const int64_t nb = n0 + c;
+                if (!row_live || nb >= a.rows) continue;
+                float v[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int64_t n = nb + j;
+                    const int64_t nn = n < a.rows ? n : a.rows - 1;
+                    const float product = __fmul_rn(__int2float_rn(static_cast<int>(r[j])), token_scale);
+                    const float result = __fmaf_rn(product, __ldg(a.ws + nn), 0.0f);
+                    v[j] = __fadd_rn(result, a.bias ? __ldg(a.bias + nn) : 0.0f);
+                }
+                if (vec && nb + 32 <= a.rows) {
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4)
+                        *reinterpret_cast<float4*>(out + nb + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (nb + j < a.rows) out[nb + j] = v[j];
+                }
+            }
+            tcgen05_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[acc]);
+        }
+    }
+
+    tcgen05_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tcgen05_fence_after();
+        tmem_dealloc(tmem_base, kTmemCols);
+    }
+}
+
+// ------------------------------------------------------------ tensor maps
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                             &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// 2-D int8 map over a row-major [outer, inner] matrix, box [box_outer, 128].
+int make_map(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, int box_outer) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) {
+        set_error("cuTensorMapEncodeTiled is not available from the driver");
+        return LEAFQ_ERR_CUDA;
+    }
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(inner)};
+    const cuuint32_t box[2] = {BK, static_cast<cuuint32_t>(box_outer)};
+    const cuuint32_t estrides[2] = {1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
+                          box, estrides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("cuTensorMapEncodeTiled failed with CUresult " + std::to_string(static_cast<int>(r)));
+        return LEAFQ_ERR_CUDA;
+    }
+    return LEAFQ_OK;
+}
+
+}  // namespace
+
+bool gemm_tc_supported(int64_t tokens, int64_t cols, int64_t rows, int bits, int64_t group,
+                       const void* weight) {
+    (void)tokens;
+    (void)rows;
+    return bits == 8 && group == cols && cols % 16 == 0 && cols >= BK && aligned16(weight);
+}
+
+int launch_gemm_tc(cudaStream_t s, const int8_t* q, const float* sx, int64_t tokens, int64_t cols,
+                   const int8_t* weight, const float* wscales, int64_t rows, const float* bias,
+                   float* y, bool pdl) {
+    if (tokens == 0 || rows == 0) return LEAFQ_OK;
+    if (!aligned16(q) || !aligned16(weight) || cols % 16 != 0) return LEAFQ_ERR_UNSUPPORTED;
+    CUtensorMap map_q, map_w;
+    int st = make_map(&map_q, q, cols, tokens, BM);
+    if (st) return st;
+    st = make_map(&map_w, weight, cols, rows, BN);
+    if (st) return st;
+    GemmArgs a;
+    a.sx = sx;
+    a.ws = wscales;
+    a.bias = bias;
+    a.y = y;
+    a.tokens = tokens;
+    a.rows = rows;
+    a.cols = cols;
+    a.m_tiles = static_cast<int>((tokens + BM - 1) / BM);
+    a.n_tiles = static_cast<int>((rows + BN - 1) / BN);
+    const int64_t tiles = (int64_t)a.m_tiles * a.n_tiles;
+    const int grid = static_cast<int>(std::min<int64_t>(tiles, sm_count()));
+    st = allow_smem(reinterpret_cast<const void*>(gemm_w8a8_tc_kernel), kSmemBytes, "gemm_w8a8_tc");
+    if (st) return st;
+    return launch(gemm_w8a8_tc_kernel, dim3(grid), dim3(kThreads), kSmemBytes, s, pdl,
+                  "gemm_w8a8_tc", map_q, map_w, a);
+}
+
+}  // namespace leafq

@@ -43,6 +43,19 @@ lr::Weight harness_weight(const void* data, const float* scales, std::size_t row
     return w;
 }
 
+// One persistent pool per thread count, like the decoder's own member pool
+// (Decoder::Impl::workers); callers use the harness from one thread.
+lr::Workers& harness_pool(unsigned threads) {
+    static std::unique_ptr<lr::Workers> pool;
+    static unsigned pool_threads = 0;
+    if (!pool || pool_threads != threads) {
+        pool.reset();
+        pool = std::make_unique<lr::Workers>(threads);
+        pool_threads = threads;
+    }
+    return *pool;
+}
+
 bool harness_vnni_available() {
 #if LEAF_DECODER_VNNI
     return __builtin_cpu_supports("avx2") && __builtin_cpu_supports("fma") &&
@@ -121,7 +134,7 @@ int leafref_linear_int(const float* x, std::size_t tokens, std::size_t cols,
                             std::lrint(x[t * cols + col] / scales[t]))));
             }
         }
-        lr::Workers workers(threads);
+        lr::Workers& workers = harness_pool(threads);
         auto bias_at = [&](std::size_t row) { return bias ? bias[row] : 0.0f; };
         workers.run(rows, [&](std::size_t first, std::size_t last) {
             std::size_t row = first;
@@ -179,7 +192,7 @@ int leafref_linear_float(const float* x, std::size_t tokens, std::size_t cols,
                          unsigned threads, int mode) {
     try {
         lr::Weight w = harness_weight(wdata, wscales, rows, cols, bits, group);
-        lr::Workers workers(threads);
+        lr::Workers& workers = harness_pool(threads);
         workers.run(rows, [&](std::size_t first, std::size_t last) {
             float result[4];
             for (std::size_t row = first; row < last; ++row)

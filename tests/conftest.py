@@ -1,0 +1,40 @@
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+REPO = Path(__file__).resolve().parents[1]
+GOLDEN = REPO / "tests" / "golden"
+if str(REPO) not in sys.path:
+    sys.path.insert(0, str(REPO))
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA (B200, sm_100a) device")
+
+
+def golden(name: str) -> dict:
+    with np.load(GOLDEN / f"{name}.npz") as data:
+        return {key: data[key] for key in data.files}
+
+
+def linear_cases():
+    return sorted(p.stem for p in GOLDEN.glob("w*.npz"))
+
+
+def bits_equal(a, b) -> bool:
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    b = np.ascontiguousarray(b, dtype=np.float32)
+    return a.shape == b.shape and np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+@pytest.fixture(scope="session")
+def cuda_device():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.fail("GPU test collected on a machine without CUDA")
+    major, minor = torch.cuda.get_device_capability(0)
+    if (major, minor) != (10, 0):
+        pytest.fail(f"leafq kernels are built for sm_100a; device is sm_{major}{minor}")
+    return torch.device("cuda", 0)
