@@ -43,7 +43,57 @@ def parse():
     p.add_argument("--cpu-seconds", type=float, default=12.0,
                    help="bounded CPU-baseline sample (rank 0, N=1)")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--case", choices=sorted(CASES),
+                   help="run one small single-kernel case three times and exit (for ncu captures)")
     return p.parse_args()
+
+
+def _case_weight(rows, cols, bits, group, device):
+    import torch
+
+    import leaf_b200 as lq
+    from leaf_b200.stack import random_w8_weight
+
+    gen = torch.Generator(device=device)
+    gen.manual_seed(0)
+    if bits == 8:
+        return random_w8_weight(rows, cols, gen, device)
+    rng = np.random.default_rng(0)
+    packed = rng.integers(0, 256, (rows, cols // 2), dtype=np.uint8)
+    scales = (rng.random((rows, cols // group), dtype=np.float32) * 1e-3 + 1e-4).astype(np.float32)
+    return lq.QuantWeight.from_host(packed, scales, rows, cols, 4, group, device=device)
+
+
+# name: (tokens, rows, cols, weight bits, group, activation bits)
+CASES = {
+    "gemv": (1, 11264, 2048, 8, 2048, 8),       # gate|up decode GEMV, 23 MB
+    "lmhead": (1, 32000, 2048, 8, 2048, 8),     # lm_head decode GEMV, 65.5 MB
+    "gemm": (512, 5632, 2048, 8, 2048, 8),      # config 2 prefill GEMM
+    "gemm_down": (512, 2048, 5632, 8, 5632, 8),  # config 2 down_proj shape
+    "gemm_big": (4096, 5632, 2048, 8, 2048, 8),  # large-M prefill
+    "w4": (1, 11008, 4096, 4, 32, 32),          # config 1 INT4 weight-only GEMV
+}
+
+
+def run_case(name):
+    import torch
+
+    import leaf_b200 as lq
+
+    tokens, rows, cols, bits, group, abits = CASES[name]
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    w = _case_weight(rows, cols, bits, group, device)
+    x = torch.randn(tokens, cols, device=device)
+    y = torch.empty(tokens, rows, device=device)
+    ws = lq.Workspace(device)
+    for _ in range(3):
+        lq.linear(x, w, activation_bits=abits, out=y, workspace=ws)
+    torch.cuda.synchronize()
+    if lq.load().leafq_device_status() != 0:
+        raise RuntimeError("device status not ok")
+    print(json.dumps({"case": name, "tokens": tokens, "rows": rows, "cols": cols, "bits": bits,
+                      "group": group, "activation_bits": abits, "status": "ok"}))
 
 
 def measured_peaks():
@@ -326,6 +376,9 @@ def read_traffic():
 
 def main():
     args = parse()
+    if args.case:
+        run_case(args.case)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

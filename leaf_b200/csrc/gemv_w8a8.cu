@@ -32,7 +32,11 @@ constexpr int kConsumerWarps = 8;
 constexpr int kRowsPerStage = kConsumerWarps;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kChunkMax = 4096;
-constexpr int kSmemBudget = 208 * 1024;
+// About half an SM's shared memory, so that under programmatic dependent
+// launch the next GEMV's block fits beside this one and starts its weight
+// stream before this one ends.  96 KB in flight per SM is still well above
+// what the HBM latency-bandwidth product needs (~40 KB per SM).
+constexpr int kSmemBudget = 100 * 1024;
 constexpr int kCodeBytesMax = 64 * 1024;
 
 struct GemvArgs {
@@ -111,19 +115,49 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_w8a8_kernel(const GemvArgs a
     }
 
     // -------------------------------------------------------- consumers
-    grid_dependency_wait();
     const int tid = threadIdx.x;
     const int nthreads = kConsumerWarps * 32;
-    // Per-token absmax (exact, order-free), scale and multiplier.
+    // Weight scales and bias are read-only: fetch this warp's rows (row
+    // row0 + 8 * rb + warp sits in lane rb) before waiting for x.
+    float row_scale = 0.0f, row_bias = 0.0f;
+    const bool rows_in_regs = nblocks <= 32;
+    if (rows_in_regs && lane < nblocks) {
+        const int64_t r = row0 + (int64_t)lane * kRowsPerStage + warp;
+        if (r < row1) {
+            row_scale = __ldg(a.ws + r);
+            row_bias = a.bias ? __ldg(a.bias + r) : 0.0f;
+        }
+    }
+    grid_dependency_wait();
+    // Per-token absmax (exact, order-free), scale and multiplier.  With one
+    // or two tokens and cols <= 8192, x stays in registers between the
+    // absmax pass and the coding pass (one read of x instead of two).
+    constexpr int kXRegs = MAXT <= 2 ? 8 : 1;
+    const int64_t vecs = a.cols / 4;
+    const bool x_in_regs = MAXT <= 2 && vecs <= (int64_t)kXRegs * nthreads;
+    float4 xr[MAXT][kXRegs];
     float m[MAXT];
 #pragma unroll
     for (int t = 0; t < MAXT; ++t) {
         m[t] = 0.0f;
         if (t < a.tokens) {
             const float4* in4 = reinterpret_cast<const float4*>(a.x + t * a.cols);
-            for (int64_t i = tid; i < a.cols / 4; i += nthreads) {
-                const float4 v = __ldg(in4 + i);
-                m[t] = fmaxf(m[t], fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+            if (x_in_regs) {
+#pragma unroll
+                for (int j = 0; j < kXRegs; ++j) {
+                    const int64_t i = tid + (int64_t)j * nthreads;
+                    xr[t][j] = i < vecs ? __ldg(in4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+                for (int j = 0; j < kXRegs; ++j) {
+                    const float4 v = xr[t][j];
+                    m[t] = fmaxf(m[t], fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+                }
+            } else {
+                for (int64_t i = tid; i < vecs; i += nthreads) {
+                    const float4 v = __ldg(in4 + i);
+                    m[t] = fmaxf(m[t], fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+                }
             }
         }
 #pragma unroll
@@ -144,12 +178,24 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_w8a8_kernel(const GemvArgs a
 #pragma unroll
     for (int t = 0; t < MAXT; ++t) {
         if (t < a.tokens) {
-            const float4* in4 = reinterpret_cast<const float4*>(a.x + t * a.cols);
             char4* out4 = reinterpret_cast<char4*>(codes + t * a.qstride);
-            for (int64_t i = tid; i < a.cols / 4; i += nthreads) {
-                const float4 v = __ldg(in4 + i);
-                out4[i] = make_char4(to_code(v.x, multiplier[t]), to_code(v.y, multiplier[t]),
-                                     to_code(v.z, multiplier[t]), to_code(v.w, multiplier[t]));
+            const float mul = multiplier[t];
+            if (x_in_regs) {
+#pragma unroll
+                for (int j = 0; j < kXRegs; ++j) {
+                    const int64_t i = tid + (int64_t)j * nthreads;
+                    const float4 v = xr[t][j];
+                    if (i < vecs)
+                        out4[i] = make_char4(to_code(v.x, mul), to_code(v.y, mul), to_code(v.z, mul),
+                                             to_code(v.w, mul));
+                }
+            } else {
+                const float4* in4 = reinterpret_cast<const float4*>(a.x + t * a.cols);
+                for (int64_t i = tid; i < vecs; i += nthreads) {
+                    const float4 v = __ldg(in4 + i);
+                    out4[i] = make_char4(to_code(v.x, mul), to_code(v.y, mul), to_code(v.z, mul),
+                                         to_code(v.w, mul));
+                }
             }
         }
     }
@@ -187,6 +233,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_w8a8_kernel(const GemvArgs a
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[buf]);
         }
+        const float sw_rb = __shfl_sync(0xffffffffu, row_scale, rb & 31);
+        const float bias_rb = __shfl_sync(0xffffffffu, row_bias, rb & 31);
         if (live) {
             int mine = 0;
 #pragma unroll
@@ -196,9 +244,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_w8a8_kernel(const GemvArgs a
                 if (lane == t) mine = acc[t];
             }
             if (lane < a.tokens) {
+                const float sw = rows_in_regs ? sw_rb : __ldg(a.ws + row);
+                const float bias = rows_in_regs ? bias_rb : (a.bias ? __ldg(a.bias + row) : 0.0f);
                 const float product = __fmul_rn(__int2float_rn(mine), token_scale[lane]);
-                const float result = __fmaf_rn(product, __ldg(a.ws + row), 0.0f);
-                const float bias = a.bias ? __ldg(a.bias + row) : 0.0f;
+                const float result = __fmaf_rn(product, sw, 0.0f);
                 a.y[(int64_t)lane * a.rows + row] = __fadd_rn(result, bias);
             }
         }
