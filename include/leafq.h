@@ -116,6 +116,23 @@ int leafq_gemm_i8_per_channel(void* stream, const int8_t* a, const int8_t* b, co
                               float input_scale, const float* weight_scales, float* out,
                               int64_t m, int64_t k, int64_t n, int activation);
 
+/* Per-row W8A8 linear (INT8 weights, group == cols, cols a multiple of 16
+ * and >= 128) that allocates nothing: for callers that cannot allocate
+ * device memory -- a plugin whose host runtime owns all device memory, a
+ * serving loop that may not touch the allocator after start-up, an embedder
+ * with a fixed budget -- and so cannot hand leafq_linear a workspace.  No
+ * counterpart in the reference (its CPU decoder reuses host vectors).
+ * Same results as leafq_linear for the same inputs.  Its scratch is a
+ * library-owned device array of 8 MiB of codes plus 16384 token scales,
+ * held on every GPU that loads the library until exit: calls with
+ * tokens * cols > 8 MiB or tokens > 16384 return LEAFQ_ERR_INVALID.  The
+ * first call on a device looks up the array's address (make it before any
+ * stream capture).  All calls share the array: calls that overlap on the
+ * GPU race; calls ordered on one stream do not. */
+int leafq_linear_w8a8_static_scratch(void* stream, const float* x, int64_t tokens, int64_t cols,
+                                     const int8_t* weight, const float* weight_scales,
+                                     int64_t rows, const float* bias, float* y, uint32_t flags);
+
 #ifdef __cplusplus
 }
 #endif

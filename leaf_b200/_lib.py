@@ -43,6 +43,8 @@ _SIGNATURES = {
     "leafq_graph_quantize": ([_vp, _vp, _i64, _f32, _vp, _vp], _int),
     "leafq_gemm_i8_per_channel": ([_vp, _vp, _vp, _vp, _f32, _vp, _vp, _i64, _i64, _i64, _int],
                                   _int),
+    "leafq_linear_w8a8_static_scratch": ([_vp, _vp, _i64, _i64, _vp, _vp, _i64, _vp, _vp, _u32],
+                                         _int),
 }
 
 _lib = None
