@@ -3,9 +3,10 @@
 
 One step = one decode token through every W8A8 Linear of a TinyLlama-1.1B
 shaped decoder (22 layers x [q|k|v, o, gate|up, down] + lm_head, batch 1,
-1.04 GB of INT8 weights, inputs larger than L2), replayed as a CUDA graph of
-leafq GEMV launches.  With --gpus N each rank runs its own replica (an
-independent request stream); value is the sum over ranks.
+1.04 GB of INT8 weights, inputs larger than L2), replayed as a CUDA graph
+holding one persistent leafq decode launch (leafq_decode_plan_run).  With
+--gpus N each rank runs its own replica (an independent request stream);
+value is the sum over ranks.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -259,8 +260,21 @@ def run_ours(args, rank, world, local_rank):
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     stack = LinearStack(tokens=1, seed=1234 + rank, device=device)
+    # Reference point: the same step as one leafq_linear launch per linear
+    # (89 launches, programmatic dependent launch), CUDA events, 20 replays.
     stack.capture(pdl=True)
-    launches = stack.launches_per_step()
+    for _ in range(3):
+        stack.graph.replay()
+    p_start, p_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p_start.record()
+    for _ in range(20):
+        stack.graph.replay()
+    p_end.record()
+    torch.cuda.synchronize(device)
+    per_linear_ms = p_start.elapsed_time(p_end) / 20
+    # The measured path: the whole step as one persistent launch.
+    stack.capture_persistent()
+    launches = stack.launches_per_step(persistent=True)
     step_bytes = stack.shape.step_bytes(1)
 
     def barrier():
@@ -343,7 +357,7 @@ def run_ours(args, rank, world, local_rank):
             "roofline": {
                 "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "traffic": traffic,
-                "kernel": "gemv_w8a8_kernel<1> (the step's only kernel; 89 launches per step)",
+                "kernel": "decode_persistent_kernel (the step's only kernel; one launch per step)",
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                 else "fallback 6650 GB/s",
                 "algorithmic_bytes_per_step": step_bytes,
@@ -353,6 +367,7 @@ def run_ours(args, rank, world, local_rank):
                     "d2h_bytes_per_step": int(stack.logits.numel() * 4),
                     "ms_per_step": e2e_ms_step},
             "gpu_launches": launches * args.steps,
+            "per_linear_launch_ms_per_step": per_linear_ms,
             "clocks": clocks,
             "cpu_baseline": cpu,
             "when": datetime.datetime.now(datetime.timezone.utc).isoformat(timespec="seconds"),

@@ -116,6 +116,38 @@ int leafq_gemm_i8_per_channel(void* stream, const int8_t* a, const int8_t* b, co
                               float input_scale, const float* weight_scales, float* out,
                               int64_t m, int64_t k, int64_t n, int activation);
 
+/* ------------------------------------------------------------------------
+ * Persistent decode step.  The reference's forward loop calls linear() for
+ * q, k, v, o, up, gate, down of every layer and lm_head
+ * (decoder.cpp:1321-1441), each on the previous call's output.  A plan
+ * holds such a chain of per-row W8A8 linears (one token); one run executes
+ * the whole chain in a single cooperative launch whose blocks stream every
+ * weight continuously and wait on each other only for activations.  Results
+ * are bit-identical to calling leafq_linear op by op. */
+typedef struct leafq_decode_op {
+    const float* x;            /* fp32 [cols], written by op `wait` (or ready at launch) */
+    float* y;                  /* fp32 [rows] */
+    const void* weight;        /* int8 [rows, cols], per-row scales */
+    const float* weight_scales;/* fp32 [rows] */
+    const float* bias;         /* fp32 [rows] or NULL */
+    int64_t rows;
+    int64_t cols;              /* multiple of 16, at most 8192 */
+    int32_t wait;              /* index of an earlier op that produces x, or -1 */
+    int32_t reserved;          /* 0 */
+} leafq_decode_op;
+
+typedef struct leafq_decode_plan_t leafq_decode_plan_t;
+
+/* Validates the ops and copies them (plus one completion counter per op) to
+ * device memory of the current device; set-up time only.  tokens must be 1. */
+int leafq_decode_plan_create(const leafq_decode_op* ops, int nops, int tokens,
+                             leafq_decode_plan_t** plan);
+/* Runs the whole chain on `stream` (a counter reset and one cooperative
+ * launch, both capturable in a CUDA graph).  Waits are bounded: a stuck
+ * dependency ends the kernel and leafq_device_status() reports it. */
+int leafq_decode_plan_run(void* stream, leafq_decode_plan_t* plan);
+int leafq_decode_plan_destroy(leafq_decode_plan_t* plan);
+
 /* Per-row W8A8 linear (INT8 weights, group == cols, cols a multiple of 16
  * and >= 128) that allocates nothing: for callers that cannot allocate
  * device memory -- a plugin whose host runtime owns all device memory, a

@@ -45,7 +45,18 @@ _SIGNATURES = {
                                   _int),
     "leafq_linear_w8a8_static_scratch": ([_vp, _vp, _i64, _i64, _vp, _vp, _i64, _vp, _vp, _u32],
                                          _int),
+    "leafq_decode_plan_create": ([_vp, _int, _int, _vp], _int),
+    "leafq_decode_plan_run": ([_vp, _vp], _int),
+    "leafq_decode_plan_destroy": ([_vp], _int),
 }
+
+
+class DecodeOp(ctypes.Structure):
+    """leafq_decode_op (include/leafq.h)."""
+
+    _fields_ = [("x", _vp), ("y", _vp), ("weight", _vp), ("weight_scales", _vp), ("bias", _vp),
+                ("rows", _i64), ("cols", _i64), ("wait", ctypes.c_int32),
+                ("reserved", ctypes.c_int32)]
 
 _lib = None
 

@@ -38,6 +38,9 @@ enum WaitSite : unsigned {
     kSiteGemmAccEmpty = 6,
     kSiteW4Full = 7,
     kSiteW4Empty = 8,
+    kSiteDecodeFull = 9,
+    kSiteDecodeEmpty = 10,
+    kSiteDecodeDependency = 11,
 };
 
 __device__ __forceinline__ unsigned long long global_timer_ns() {

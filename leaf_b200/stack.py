@@ -102,8 +102,42 @@ class LinearStack:
         self.logits = torch.empty((t, shape.vocab), device=self.device)
         self.graph = None
 
-    def launches_per_step(self) -> int:
-        return 4 * self.shape.layers + 1
+    def launches_per_step(self, persistent: bool = True) -> int:
+        return 1 if persistent else 4 * self.shape.layers + 1
+
+    def plan_ops(self):
+        """The step as a decode-plan chain: (x, weight, y, wait) per linear."""
+        h, f = self.shape.hidden, self.shape.intermediate
+        ops = []
+        x, wait = self.x, -1
+        for layer in self.layers:
+            base = len(ops)
+            ops.append((x, layer["qkv"], self.qkv, wait))
+            ops.append((self.qkv[:, :h], layer["o"], self.o, base))
+            ops.append((self.o, layer["gate_up"], self.gate_up, base + 1))
+            ops.append((self.gate_up[:, f:], layer["down"], self.down, base + 2))
+            x, wait = self.down, base + 3
+        ops.append((x, self.lm_head, self.logits, wait))
+        return ops
+
+    def run_persistent(self) -> torch.Tensor:
+        """One step as a single persistent launch (the bench path)."""
+        from .decode import DecodePlan
+
+        if getattr(self, "plan", None) is None:
+            if self.tokens != 1:
+                raise ValueError("the persistent decode kernel runs one token per step")
+            self.plan = DecodePlan(self.plan_ops())
+        self.plan.run()
+        return self.logits
+
+    def capture_persistent(self) -> None:
+        self.run_persistent()  # plan creation and kernel attributes outside capture
+        torch.cuda.synchronize(self.device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.plan.run()
+        torch.cuda.synchronize(self.device)
 
     def _step(self, flags: int) -> None:
         h, f = self.shape.hidden, self.shape.intermediate
