@@ -122,29 +122,32 @@ int leafq_gemm_i8_per_channel(void* stream, const int8_t* a, const int8_t* b, co
  * (decoder.cpp:1321-1441), each on the previous call's output.  A plan
  * holds such a chain of per-row W8A8 linears (one token); one run executes
  * the whole chain in a single cooperative launch whose blocks stream every
- * weight continuously and wait on each other only for activations.  Results
- * are bit-identical to calling leafq_linear op by op. */
+ * weight continuously and hand activations to each other through tagged
+ * words in plan-owned buffers.  Results are bit-identical to calling
+ * leafq_linear op by op. */
 typedef struct leafq_decode_op {
-    const float* x;            /* fp32 [cols], written by op `wait` (or ready at launch) */
-    float* y;                  /* fp32 [rows] */
+    const float* x;            /* fp32 [cols] ready at launch when wait == -1, else NULL */
+    float* y;                  /* fp32 [rows] copy of the output for the caller, or NULL */
     const void* weight;        /* int8 [rows, cols], per-row scales */
     const float* weight_scales;/* fp32 [rows] */
     const float* bias;         /* fp32 [rows] or NULL */
     int64_t rows;
     int64_t cols;              /* multiple of 16, at most 8192 */
-    int32_t wait;              /* index of an earlier op that produces x, or -1 */
-    int32_t reserved;          /* 0 */
+    int32_t wait;              /* earlier op whose output is this op's x, or -1 */
+    int32_t x_offset;          /* first element of that output used as x (multiple of 4) */
 } leafq_decode_op;
 
 typedef struct leafq_decode_plan_t leafq_decode_plan_t;
 
-/* Validates the ops and copies them (plus one completion counter per op) to
- * device memory of the current device; set-up time only.  tokens must be 1. */
+/* Validates the ops, copies them to device memory of the current device and
+ * allocates the buffers that carry outputs to later ops; set-up time only.
+ * tokens must be 1, at most 160 ops. */
 int leafq_decode_plan_create(const leafq_decode_op* ops, int nops, int tokens,
                              leafq_decode_plan_t** plan);
-/* Runs the whole chain on `stream` (a counter reset and one cooperative
- * launch, both capturable in a CUDA graph).  Waits are bounded: a stuck
- * dependency ends the kernel and leafq_device_status() reports it. */
+/* Runs the whole chain on `stream` as one cooperative launch (capturable in
+ * a CUDA graph).  Runs of one plan must be ordered (one stream).  Waits are
+ * bounded: a stuck hand-off ends the kernel and leafq_device_status()
+ * reports it; destroy and recreate the plan after such an error. */
 int leafq_decode_plan_run(void* stream, leafq_decode_plan_t* plan);
 int leafq_decode_plan_destroy(leafq_decode_plan_t* plan);
 

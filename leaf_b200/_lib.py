@@ -56,7 +56,7 @@ class DecodeOp(ctypes.Structure):
 
     _fields_ = [("x", _vp), ("y", _vp), ("weight", _vp), ("weight_scales", _vp), ("bias", _vp),
                 ("rows", _i64), ("cols", _i64), ("wait", ctypes.c_int32),
-                ("reserved", ctypes.c_int32)]
+                ("x_offset", ctypes.c_int32)]
 
 _lib = None
 

@@ -66,6 +66,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_w4a32_kernel(const W4Args a)
     float* SC = P + kRowsPerStage * (G + 1);
     uint64_t* full = reinterpret_cast<uint64_t*>(SC + kRowsPerStage * (G + 1));
     uint64_t* empty = full + S;
+    // Raised when a wait gives up; consumers keep arriving at every block
+    // barrier and return together after it.
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + S);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t row0 = (int64_t)blockIdx.x * a.rows / gridDim.x;
@@ -77,6 +80,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_w4a32_kernel(const W4Args a)
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kConsumers / 32);
         }
+        *abort_flag = 0;
         fence_barrier_init();
     }
     __syncthreads();
@@ -122,10 +126,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_w4a32_kernel(const W4Args a)
         const int buf = s % S;
         const int64_t r0 = row0 + (int64_t)s * kRowsPerStage;
         const int live = static_cast<int>(min64(kRowsPerStage, row1 - r0));
-        if (!mbar_wait(&full[buf], (s / S) & 1, kSiteW4Full)) return;
+        const bool landed = mbar_wait(&full[buf], (s / S) & 1, kSiteW4Full);
+        if (!landed) *abort_flag = 1;
         const uint8_t* sw = stages + (size_t)buf * stage_bytes;
         const float* sscale = reinterpret_cast<const float*>(sw + w_bytes);
-        if (active) {
+        if (landed && active) {
             for (int r = slot; r < live; r += slots) {
                 const uint4* packed =
                     reinterpret_cast<const uint4*>(sw + (size_t)r * row_bytes + (size_t)g * (GS / 2));
@@ -161,6 +166,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_w4a32_kernel(const W4Args a)
             }
         }
         consumer_sync();
+        if (*abort_flag) return;
         if (lane == 0) mbar_arrive(&empty[buf]);
         if (tid < live) {
             float result = 0.0f;
@@ -220,7 +226,7 @@ int launch_gemv_w4a32_fast(cudaStream_t s, const float* x, int64_t cols, const u
                         static_cast<int64_t>(stage_bytes + 16);
     if (fit < 1) return LEAFQ_ERR_UNSUPPORTED;
     a.stages = static_cast<int>(std::min<int64_t>(fit, max_stages));
-    const size_t smem = stage_bytes * a.stages + fixed + 16 * a.stages;
+    const size_t smem = stage_bytes * a.stages + fixed + 16 * a.stages + 16;  // + abort flag
     switch (group) {
         case 32: return launch_gs<32>(s, a, grid, smem, pdl);
         case 64: return launch_gs<64>(s, a, grid, smem, pdl);

@@ -106,18 +106,21 @@ class LinearStack:
         return 1 if persistent else 4 * self.shape.layers + 1
 
     def plan_ops(self):
-        """The step as a decode-plan chain: (x, weight, y, wait) per linear."""
-        h, f = self.shape.hidden, self.shape.intermediate
+        """The step as a decode-plan chain (same dependencies as _step)."""
+        from .decode import DecodeOp
+
+        f = self.shape.intermediate
         ops = []
-        x, wait = self.x, -1
-        for layer in self.layers:
+        for i, layer in enumerate(self.layers):
             base = len(ops)
-            ops.append((x, layer["qkv"], self.qkv, wait))
-            ops.append((self.qkv[:, :h], layer["o"], self.o, base))
-            ops.append((self.o, layer["gate_up"], self.gate_up, base + 1))
-            ops.append((self.gate_up[:, f:], layer["down"], self.down, base + 2))
-            x, wait = self.down, base + 3
-        ops.append((x, self.lm_head, self.logits, wait))
+            if i == 0:
+                ops.append(DecodeOp(layer["qkv"], x=self.x))
+            else:
+                ops.append(DecodeOp(layer["qkv"], wait=base - 1))
+            ops.append(DecodeOp(layer["o"], wait=base))                    # q slice of q|k|v
+            ops.append(DecodeOp(layer["gate_up"], wait=base + 1))
+            ops.append(DecodeOp(layer["down"], wait=base + 2, x_offset=f))  # up half of gate|up
+        ops.append(DecodeOp(self.lm_head, wait=len(ops) - 1, y=self.logits))
         return ops
 
     def run_persistent(self) -> torch.Tensor:
