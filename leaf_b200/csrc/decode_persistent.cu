@@ -108,6 +108,22 @@ __device__ __forceinline__ OpGeometry geometry(const Op& op) {
     return g;
 }
 
+// Scale and bias of row block (group + 2 * lane), row wi, of `op` for this
+// warp (zero when the lane has no such row or the op has over 64 blocks, in
+// which case the epilogue reads them directly).
+__device__ __forceinline__ void load_row_params(const Op& op, const OpGeometry& g, int group, int wi,
+                                                int lane, float& scale, float& bias) {
+    scale = 0.0f;
+    bias = 0.0f;
+    if (g.nblocks <= 2 * 32 && group + 2 * lane < g.nblocks) {
+        const int64_t r = g.row0 + (int64_t)(group + 2 * lane) * kRowsPerStage + wi;
+        if (r < g.row1) {
+            scale = __ldg(op.ws + r);
+            bias = op.bias ? __ldg(op.bias + r) : 0.0f;
+        }
+    }
+}
+
 __device__ __forceinline__ int block_rows(const OpGeometry& g, int rb) {
     return static_cast<int>(min64(kRowsPerStage, g.row1 - g.row0 - (int64_t)rb * kRowsPerStage));
 }
@@ -211,19 +227,28 @@ decode_persistent_kernel(const Op* __restrict__ ops_global, int nops, uint32_t* 
     int s = 0;
     RingCursor cursor;
     bool ok = true;
+    int prefetched_j = -1;
+    float next_scale = 0.0f, next_bias = 0.0f;
     for (int j = 0; j < nops; ++j) {
         const Op& op = ops[j];
         const OpGeometry g = geometry(op);
         if (g.nblocks == 0) continue;  // no rows here: nothing to read or write
-        // Row scale / bias of this warp's k-th row block (group + 2k) in lane k.
+        // Row scale / bias of this warp's k-th row block (group + 2k) in lane
+        // k, loaded one linear ahead so the epilogue never waits for them.
         const bool rows_in_regs = g.nblocks <= 2 * 32;
-        float row_scale = 0.0f, row_bias = 0.0f;
-        if (rows_in_regs && group + 2 * lane < g.nblocks) {
-            const int64_t r = g.row0 + (int64_t)(group + 2 * lane) * kRowsPerStage + wi;
-            if (r < g.row1) {
-                row_scale = __ldg(op.ws + r);
-                row_bias = op.bias ? __ldg(op.bias + r) : 0.0f;
-            }
+        float row_scale, row_bias;
+        if (prefetched_j == j) {
+            row_scale = next_scale;
+            row_bias = next_bias;
+        } else {
+            load_row_params(op, g, group, wi, lane, row_scale, row_bias);
+        }
+        for (int j2 = j + 1; j2 < nops; ++j2) {
+            const OpGeometry g2 = geometry(ops[j2]);
+            if (g2.nblocks == 0) continue;
+            load_row_params(ops[j2], g2, group, wi, lane, next_scale, next_bias);
+            prefetched_j = j2;
+            break;
         }
         // x into registers: plain fp32, or tagged words (spin until tagged).
         const int64_t vecs = op.cols / 4;

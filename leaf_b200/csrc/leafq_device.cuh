@@ -41,6 +41,7 @@ enum WaitSite : unsigned {
     kSiteDecodeFull = 9,
     kSiteDecodeEmpty = 10,
     kSiteDecodeDependency = 11,
+    kSiteDecodeCodes = 12,
 };
 
 __device__ __forceinline__ unsigned long long global_timer_ns() {
