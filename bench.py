@@ -73,6 +73,7 @@ CASES = {
     "gemm_down": (512, 2048, 5632, 8, 5632, 8),  # config 2 down_proj shape
     "gemm_big": (4096, 5632, 2048, 8, 2048, 8),  # large-M prefill
     "w4": (1, 11008, 4096, 4, 32, 32),          # config 1 INT4 weight-only GEMV
+    "decode_small": None,                        # persistent decode kernel, 3-layer stack
 }
 
 
@@ -81,6 +82,21 @@ def run_case(name):
 
     import leaf_b200 as lq
 
+    if name == "decode_small":
+        # The persistent decode kernel on a 3-layer TinyLlama-width stack
+        # (132 MB of weights: larger than L2, small enough for ncu replays).
+        from leaf_b200.stack import LinearStack, StackShape
+
+        torch.cuda.set_device(0)
+        stack = LinearStack(StackShape(layers=3))
+        for _ in range(3):
+            stack.run_persistent()
+        torch.cuda.synchronize()
+        if lq.load().leafq_device_status() != 0:
+            raise RuntimeError("device status not ok")
+        print(json.dumps({"case": name, "layers": 3, "step_bytes": stack.shape.step_bytes(1),
+                          "status": "ok"}))
+        return
     tokens, rows, cols, bits, group, abits = CASES[name]
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
@@ -377,7 +393,7 @@ def run_ours(args, rank, world, local_rank):
 
 def read_traffic():
     """DRAM bytes per decode step from the committed ncu summary, if any."""
-    path = REPO / "profiles" / "gemv_w8a8_decode_stack.md"
+    path = REPO / "profiles" / "decode_persistent_tinyllama_step.md"
     if not path.exists():
         return None
     for line in path.read_text().splitlines():
