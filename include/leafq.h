@@ -168,6 +168,55 @@ int leafq_linear_w8a8_static_scratch(void* stream, const float* x, int64_t token
                                      const int8_t* weight, const float* weight_scales,
                                      int64_t rows, const float* bias, float* y, uint32_t flags);
 
+/* ------------------------------------------------------------------------
+ * N-sharded linear across GPUs (one process per GPU).  Output rows are
+ * independent (the reference splits them over its worker threads,
+ * decoder.cpp:1109 / host_support.h:151-178), so rank g computes rows
+ * [row_begin, row_begin + local_rows) of every linear and the rows are
+ * gathered along N -- bit-identical to the unsharded leafq_linear.
+ *
+ * The gather runs over peer memory without NCCL: each rank's rows are
+ * stored straight into every rank's receive buffer (CUDA IPC mapping over
+ * NVLink) as flag-in-data words, by the GEMV epilogue itself on the decode
+ * path.  The reference has no multi-GPU code; these replace the
+ * all-gather step of its row partitioning. */
+#define LEAFQ_IPC_HANDLE_BYTES 64
+
+typedef struct leafq_allgather leafq_allgather_t;
+
+/* Creates this rank's side (current device = this rank's GPU): a receive
+ * buffer for up to max_elements gathered floats (2 x 8 bytes each) and a
+ * scratch of max_elements floats.  Writes the buffer's CUDA IPC handle
+ * (LEAFQ_IPC_HANDLE_BYTES) to ipc_handle; the caller exchanges the handles
+ * of all ranks (any host collective) and passes them to _connect.
+ * world 1..8. */
+int leafq_allgather_init(int rank, int world, int64_t max_elements, leafq_allgather_t** ag,
+                         void* ipc_handle);
+/* Maps the other ranks' receive buffers.  handles: world x
+ * LEAFQ_IPC_HANDLE_BYTES in rank order (this rank's entry is ignored). */
+int leafq_allgather_connect(leafq_allgather_t* ag, const void* handles);
+/* out[t, row_begin_g + j] = local_g[t, j] on every rank g, for t < tokens.
+ * local: [tokens, local_rows] fp32; out: [tokens, rows] fp32.  Every rank
+ * must make the same sequence of _run / _linear_allgather calls with the
+ * same tokens and rows; a rank that stops leaves the others waiting 2 s,
+ * after which their output is NaN and leafq_device_status reports
+ * LEAFQ_ERR_TIMEOUT. */
+int leafq_allgather_run(void* stream, leafq_allgather_t* ag, const float* local, int64_t tokens,
+                        int64_t local_rows, int64_t row_begin, int64_t rows, float* out);
+/* leafq_linear on this rank's weight rows (weight/weight_scales/bias hold
+ * local_rows rows), gathered into out [tokens, rows] on every rank.  The
+ * per-row INT8 decode GEMV (tokens <= 8) stores its rows into the peers
+ * from its epilogue; other paths run the linear into the scratch first.
+ * Workspace rules are those of leafq_linear for (tokens, cols). */
+int leafq_linear_allgather(void* stream, leafq_allgather_t* ag, const float* x, int64_t tokens,
+                           int64_t cols, const void* weight, const float* weight_scales,
+                           int64_t local_rows, int64_t row_begin, int64_t rows, int bits,
+                           int64_t group, int activation_bits, const float* bias, float* out,
+                           void* workspace, size_t workspace_bytes, uint32_t flags);
+/* Unmaps the peers and frees.  Every rank must have finished its last run
+ * (a host barrier after a device synchronise) before any rank destroys. */
+int leafq_allgather_destroy(leafq_allgather_t* ag);
+
 #ifdef __cplusplus
 }
 #endif

@@ -23,6 +23,8 @@ LEAFQ_ERR_NONFINITE = 5
 LEAFQ_FLAG_VNNI_ROUNDING = 0x1
 LEAFQ_FLAG_PDL = 0x2
 
+LEAFQ_IPC_HANDLE_BYTES = 64
+
 _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64
 _int = ctypes.c_int
@@ -48,6 +50,12 @@ _SIGNATURES = {
     "leafq_decode_plan_create": ([_vp, _int, _int, _vp], _int),
     "leafq_decode_plan_run": ([_vp, _vp], _int),
     "leafq_decode_plan_destroy": ([_vp], _int),
+    "leafq_allgather_init": ([_int, _int, _i64, _vp, _vp], _int),
+    "leafq_allgather_connect": ([_vp, _vp], _int),
+    "leafq_allgather_run": ([_vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp], _int),
+    "leafq_linear_allgather": ([_vp, _vp, _vp, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _int, _i64,
+                                _int, _vp, _vp, _vp, _size, _u32], _int),
+    "leafq_allgather_destroy": ([_vp], _int),
 }
 
 

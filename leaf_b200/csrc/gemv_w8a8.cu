@@ -52,6 +52,7 @@ struct GemvArgs {
     int nchunks;  // ceil(cols / chunk)
     int stages;   // ring depth
     int qstride;  // bytes between token rows of the code buffer
+    PeerStore peer;  // fused all-gather epilogue when peer.world > 0
 };
 
 __device__ __forceinline__ void consumer_sync() {
@@ -129,6 +130,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_w8a8_kernel(const GemvArgs a
         }
     }
     grid_dependency_wait();
+    // The run tag of a fused all-gather (written by the previous collect).
+    const uint32_t tag = a.peer.world ? *reinterpret_cast<const volatile uint32_t*>(a.peer.epoch) : 0u;
     // Per-token absmax (exact, order-free), scale and multiplier.  With one
     // or two tokens and cols <= 8192, x stays in registers between the
     // absmax pass and the coding pass (one read of x instead of two).
@@ -248,7 +251,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_w8a8_kernel(const GemvArgs a
                 const float bias = rows_in_regs ? bias_rb : (a.bias ? __ldg(a.bias + row) : 0.0f);
                 const float product = __fmul_rn(__int2float_rn(mine), token_scale[lane]);
                 const float result = __fmaf_rn(product, sw, 0.0f);
-                a.y[(int64_t)lane * a.rows + row] = __fadd_rn(result, bias);
+                const float y = __fadd_rn(result, bias);
+                if (a.peer.world)
+                    peer_store(a.peer, tag, lane, row, y);
+                else
+                    a.y[(int64_t)lane * a.rows + row] = y;
             }
         }
     }
@@ -275,9 +282,11 @@ bool gemv_w8a8_supported(int64_t tokens, int64_t cols, int bits, int64_t group,
 
 int launch_gemv_w8a8(cudaStream_t s, const float* x, int64_t tokens, int64_t cols,
                      const int8_t* weight, const float* wscales, int64_t rows, const float* bias,
-                     float* y, bool pdl) {
+                     float* y, bool pdl, const PeerStore* peer) {
     if (rows == 0 || tokens == 0) return LEAFQ_OK;
     GemvArgs a;
+    a.peer = {};
+    if (peer) a.peer = *peer;
     a.x = x;
     a.w = weight;
     a.ws = wscales;

@@ -14,6 +14,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include "leafq_internal.h"
+
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
 #error "leafq kernels are written for sm_100a only"
 #endif
@@ -42,6 +44,7 @@ enum WaitSite : unsigned {
     kSiteDecodeEmpty = 10,
     kSiteDecodeDependency = 11,
     kSiteDecodeCodes = 12,
+    kSiteAllGather = 13,
 };
 
 __device__ __forceinline__ unsigned long long global_timer_ns() {
@@ -272,6 +275,19 @@ __device__ __forceinline__ uint64_t umma_desc_k_sw128(uint32_t smem_addr) {
 // N >> 3 in [17,23), M >> 4 in [24,29).
 __host__ __device__ constexpr uint32_t umma_idesc_i8(uint32_t m, uint32_t n) {
     return (2u << 4) | (1u << 7) | (1u << 10) | ((n >> 3) << 17) | ((m >> 4) << 24);
+}
+
+// ------------------------------------------------ peer-memory all-gather
+// One flag-in-data word {value, tag} of gathered element (token, local_row),
+// stored into every rank's receive buffer.  The 8-byte store is single-copy
+// atomic, so a reader that sees the tag also sees the value; no fence.
+__device__ __forceinline__ void peer_store(const PeerStore& p, uint32_t tag, int64_t token,
+                                           int64_t local_row, float v) {
+    const int64_t idx = (int64_t)(tag & 1u) * p.half + token * p.rows + p.row_offset + local_row;
+    const unsigned long long word =
+        (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
+    for (int g = 0; g < p.world; ++g)
+        asm volatile("st.volatile.global.b64 [%0], %1;" ::"l"(p.dst[g] + idx), "l"(word) : "memory");
 }
 
 }  // namespace leafq

@@ -47,6 +47,23 @@ int allow_smem(const void* kernel, size_t bytes, const char* what);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// ------------------------------------------------ peer-memory all-gather
+// A kernel that ends an N-sharded linear can store its output rows straight
+// into every rank's receive buffer (CUDA IPC mappings over NVLink) as
+// flag-in-data words {fp32 value, 32-bit run tag}; the receiving rank polls
+// its own buffer until every word carries the current tag.  Two halves
+// alternate with the tag's parity, so a rank one run ahead never overwrites
+// words a slower rank has still to read.
+constexpr int kMaxPeers = 8;
+struct PeerStore {
+    unsigned long long* dst[kMaxPeers];  // receive buffers of ranks 0..world-1
+    const unsigned int* epoch;           // this rank's run counter = the run's tag
+    int world;                           // 0: no peer stores (plain output)
+    long long half;                      // words per parity half
+    long long row_offset;                // gathered row of local row 0
+    long long rows;                      // rows of the gathered output
+};
+
 // ------------------------------------------------------------ launchers
 // Each returns a LEAFQ_* status; arguments are validated by the caller.
 int launch_quantize_act(cudaStream_t s, const float* x, int64_t tokens, int64_t cols, int8_t* q,
@@ -55,9 +72,11 @@ int launch_quantize_act(cudaStream_t s, const float* x, int64_t tokens, int64_t 
 // Fused act-quant + per-row W8A8 GEMV for tokens <= 8 (bulk-TMA weights).
 bool gemv_w8a8_supported(int64_t tokens, int64_t cols, int bits, int64_t group,
                          const void* weight, const float* x);
+// With `peer` (world > 0) the epilogue stores into the receive buffers
+// instead of y.
 int launch_gemv_w8a8(cudaStream_t s, const float* x, int64_t tokens, int64_t cols,
                      const int8_t* weight, const float* wscales, int64_t rows, const float* bias,
-                     float* y, bool pdl);
+                     float* y, bool pdl, const PeerStore* peer = nullptr);
 
 // Generic integer linear from codes (any group, bits 8 / 4, any tokens).
 int launch_linear_int_q(cudaStream_t s, const int8_t* q, const float* sx, int64_t tokens,

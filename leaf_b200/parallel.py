@@ -17,6 +17,7 @@ NCCL is ``leafq_allgather_*`` in the C ABI (``PeerAllGather`` below).
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 from typing import Optional
 
@@ -25,8 +26,8 @@ import torch
 import torch.distributed as dist
 
 from . import _lib
-from ._lib import LeafError
-from .linear import QuantWeight, Workspace, linear
+from ._lib import LeafError, check, load
+from .linear import QuantWeight, Workspace, _ptr, _require_cuda, _stream, linear
 
 
 @dataclass(frozen=True)
@@ -109,15 +110,94 @@ class RowGather:
         return out
 
 
+class PeerAllGather:
+    """The C ABI's peer-memory all-gather (``leafq_allgather_*``) on a process
+    group of one process per GPU.
+
+    Creation is collective: every rank allocates its receive buffer for up to
+    `max_elements` gathered floats and the CUDA IPC handles are exchanged
+    over the group.  Every rank must then make the same sequence of
+    ``run`` / ``linear`` calls (same tokens and rows); they may be captured
+    in a CUDA graph.  ``close`` is collective too."""
+
+    def __init__(self, max_elements: int, group=None):
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        self.max_elements = int(max_elements)
+        lib = load()
+        handle = (ctypes.c_uint8 * _lib.LEAFQ_IPC_HANDLE_BYTES)()
+        ag = ctypes.c_void_p()
+        check(lib.leafq_allgather_init(self.rank, self.world, self.max_elements, ctypes.byref(ag),
+                                       handle))
+        self._ag = ag
+        on = self.device if dist.get_backend(group) == "nccl" else torch.device("cpu")
+        mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=on)
+        every = torch.empty(self.world * _lib.LEAFQ_IPC_HANDLE_BYTES, dtype=torch.uint8, device=on)
+        dist.all_gather_into_tensor(every, mine, group=group)
+        table = (ctypes.c_uint8 * every.numel())(*every.cpu().tolist())
+        check(lib.leafq_allgather_connect(self._ag, table))
+
+    def run(self, local: torch.Tensor, row_begin: int, rows: int,
+            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Gather [tokens, local_rows] slices (this rank's at row_begin) into
+        [tokens, rows] on every rank."""
+        _require_cuda(local, "local rows")
+        tokens, local_rows = local.shape
+        if out is None:
+            out = torch.empty((tokens, rows), dtype=torch.float32, device=local.device)
+        check(load().leafq_allgather_run(_stream(local.device), self._ag, local.data_ptr(), tokens,
+                                         local_rows, row_begin, rows, out.data_ptr()))
+        return out
+
+    def linear(self, x: torch.Tensor, shard: QuantWeight, row_begin: int, rows: int,
+               activation_bits: int = 8, out: Optional[torch.Tensor] = None,
+               workspace: Optional[Workspace] = None, flags: int = 0) -> torch.Tensor:
+        """This rank's rows of the linear, gathered into [tokens, rows] on
+        every rank; the decode GEMV stores into the peers from its epilogue."""
+        _require_cuda(x, "input")
+        if x.dtype != torch.float32 or x.dim() != 2 or x.shape[1] != shard.cols:
+            raise LeafError(_lib.LEAFQ_ERR_INVALID, "input must be float32 [tokens, cols]")
+        if shard.input_scale is not None:
+            x = (x * shard.input_scale).contiguous()
+        tokens = x.shape[0]
+        if out is None:
+            out = torch.empty((tokens, rows), dtype=torch.float32, device=x.device)
+        lib = load()
+        need = lib.leafq_linear_workspace_bytes(tokens, shard.cols, shard.bits, shard.group,
+                                                activation_bits)
+        ws_ptr, ws_bytes = None, 0
+        if need:
+            workspace = workspace or Workspace(x.device)
+            buf = workspace.get(need)
+            ws_ptr, ws_bytes = buf.data_ptr(), buf.numel()
+        check(lib.leafq_linear_allgather(
+            _stream(x.device), self._ag, x.data_ptr(), tokens, shard.cols, shard.data.data_ptr(),
+            _ptr(shard.scales), shard.rows, row_begin, rows, shard.bits, shard.group,
+            activation_bits, _ptr(shard.bias), out.data_ptr(), ws_ptr, ws_bytes, flags))
+        return out
+
+    def close(self) -> None:
+        if self._ag is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)  # no rank may still store into a buffer being freed
+        check(load().leafq_allgather_destroy(self._ag))
+        self._ag = None
+
+
 class ShardedLinear:
     """``Decoder::Impl::linear`` for one weight, N-sharded over a process group.
 
     Each rank holds rows [begin, end) of the weight on its own GPU; ``__call__``
     takes the full activation [tokens, cols] on every rank and returns the
     full output [tokens, rows] on every rank, bit-identical to the unsharded
-    call."""
+    call.  The gather is an NCCL all-gather (``RowGather``) or, given a
+    ``PeerAllGather``, the C ABI's peer-memory gather fused into the kernel."""
 
-    def __init__(self, shard: QuantWeight, rows: int, activation_bits: int = 8, group=None):
+    def __init__(self, shard: QuantWeight, rows: int, activation_bits: int = 8, group=None,
+                 peer: Optional[PeerAllGather] = None):
         self.gather = RowGather(rows, group)
         rank = self.gather.rank
         if shard.rows != self.gather.part.count(rank):
@@ -125,12 +205,15 @@ class ShardedLinear:
         self.shard = shard
         self.rows = rows
         self.cols = shard.cols
+        self.row_begin = self.gather.part.begin(rank)
         self.activation_bits = activation_bits
+        self.peer = peer
         self.workspace = Workspace(shard.data.device)
 
     @classmethod
     def from_host(cls, data, scales, rows, cols, bits, group_size, bias=None, input_scale=None,
-                  activation_bits: int = 8, group=None, device="cuda"):
+                  activation_bits: int = 8, group=None, device="cuda",
+                  peer: Optional[PeerAllGather] = None):
         """Cut the full artifact-layout weight to this rank's rows and upload them."""
         world, rank = dist.get_world_size(group), dist.get_rank(group)
         d, s, b, lo, hi = shard_host_weight(data, scales, bias, rows, cols, bits, group_size,
@@ -138,9 +221,12 @@ class ShardedLinear:
         shard = QuantWeight.from_host(d, s, hi - lo, cols, bits, group_size, b, input_scale,
                                       device=device)
         shard.check()
-        return cls(shard, rows, activation_bits, group)
+        return cls(shard, rows, activation_bits, group, peer)
 
     def __call__(self, x: torch.Tensor, out: Optional[torch.Tensor] = None,
                  flags: int = 0) -> torch.Tensor:
+        if self.peer is not None:
+            return self.peer.linear(x, self.shard, self.row_begin, self.rows, self.activation_bits,
+                                    out=out, workspace=self.workspace, flags=flags)
         local = linear(x, self.shard, self.activation_bits, workspace=self.workspace, flags=flags)
         return self.gather(local, out)
