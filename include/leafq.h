@@ -217,6 +217,59 @@ int leafq_linear_allgather(void* stream, leafq_allgather_t* ag, const float* x, 
  * (a host barrier after a device synchronise) before any rank destroys. */
 int leafq_allgather_destroy(leafq_allgather_t* ag);
 
+/* ------------------------------------------------------------------------
+ * Decoder operators around the linears (Decoder::Impl::forward_into,
+ * decoder.cpp:1282-1452), for a GPU port of the decode loop.  Device
+ * pointers, fp32 activations, token-major rows.  `position` is a device
+ * int32 holding the number of tokens already in the KV cache, so one CUDA
+ * graph serves every decode step (leafq_advance_position moves it). */
+
+/* out[t, c] = Weight::value(ids[t], c) * embedding_scale
+ * (decoder.cpp:1293-1304, :241-250); table in artifact layout (bits 8/4
+ * with group scales, or fp32).  Out-of-range ids set *error_flag (if
+ * given) and read row 0. */
+int leafq_embed(void* stream, const int32_t* ids, int64_t tokens, const void* table,
+                const float* scales, int bits, int64_t group, int64_t vocab, int64_t hidden,
+                float embedding_scale, float* out, int32_t* error_flag);
+/* RMSNorm (norm(), decoder.cpp:706-727) of each token row, optionally after
+ * the residual add hidden += delta (+ 0.0f first when add_zero, as
+ * decoder.cpp:1434 does); hidden is updated in place.  Bit-identical to the
+ * reference (sum of squares accumulated left to right). */
+int leafq_rmsnorm(void* stream, float* hidden, const float* delta, int add_zero, int64_t tokens,
+                  int64_t width, const float* weight, float epsilon, float* out);
+/* Host function: RoPE tables [positions][rotary_dim/2] with the reference's
+ * float libm calls (frequencies decoder.cpp:929-933, angles :1248-1256). */
+int leafq_rope_tables(float theta, int rotary_dim, int64_t positions, float* cos_out,
+                      float* sin_out);
+/* qkv [tokens][(heads + 2*kv_heads) * dim] (q | k | v): rotates q and k
+ * (decoder.cpp:1259-1281), writes q as [heads][tokens][dim] and appends k,
+ * v at rows position..position+tokens-1 of caches [kv_heads][capacity][dim]
+ * (kv_cache.cpp:21-59). */
+int leafq_rotary_append(void* stream, const float* qkv, int64_t tokens, int heads, int kv_heads,
+                        int dim, int rotary_dim, const float* cos_table, const float* sin_table,
+                        const int32_t* position, float* q_heads, float* k_cache, float* v_cache,
+                        int64_t capacity);
+/* Causal GQA attention of the chunk's tokens over the cache
+ * (KVCache::attend, transformer.cpp:93-145): score = (q.k * scale) * scale,
+ * softmax with libm's expf, probability-weighted V, every sum in the
+ * reference's order; out [tokens][heads * dim], bit-identical to the
+ * reference.  Keys 0..position+t for query t; (dim + capacity) * 4 bytes
+ * must fit in shared memory. */
+int leafq_attention(void* stream, const float* q_heads, const float* k_cache, const float* v_cache,
+                    int64_t tokens, int heads, int kv_heads, int dim, const int32_t* position,
+                    int64_t capacity, float scale, float* out);
+/* gate_up [tokens][2 * width] (gate | up) -> out [tokens][width] =
+ * up * (gate / (1 + expf(-gate))) (decoder.cpp:982-988, 1414). */
+int leafq_silu_gate(void* stream, const float* gate_up, int64_t tokens, int64_t width, float* out);
+/* ids[r] = first index of the largest value of logits row r
+ * (std::max_element, main_decoder.cpp:101). */
+int leafq_argmax(void* stream, const float* logits, int64_t rows, int64_t width, int32_t* ids);
+/* y[i] = expf(x[i]) bit-identical to the system libm's expf (GNU C Library
+ * 2.39), the exponential of the decoder's softmax and SiLU. */
+int leafq_expf(void* stream, const float* x, int64_t n, float* y);
+/* *position += count on the stream. */
+int leafq_advance_position(void* stream, int32_t* position, int32_t count);
+
 #ifdef __cplusplus
 }
 #endif

@@ -56,6 +56,16 @@ _SIGNATURES = {
     "leafq_linear_allgather": ([_vp, _vp, _vp, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _int, _i64,
                                 _int, _vp, _vp, _vp, _size, _u32], _int),
     "leafq_allgather_destroy": ([_vp], _int),
+    "leafq_embed": ([_vp, _vp, _i64, _vp, _vp, _int, _i64, _i64, _i64, _f32, _vp, _vp], _int),
+    "leafq_rmsnorm": ([_vp, _vp, _vp, _int, _i64, _i64, _vp, _f32, _vp], _int),
+    "leafq_rope_tables": ([_f32, _int, _i64, _vp, _vp], _int),
+    "leafq_rotary_append": ([_vp, _vp, _i64, _int, _int, _int, _int, _vp, _vp, _vp, _vp, _vp, _vp,
+                             _i64], _int),
+    "leafq_attention": ([_vp, _vp, _vp, _vp, _i64, _int, _int, _int, _vp, _i64, _f32, _vp], _int),
+    "leafq_silu_gate": ([_vp, _vp, _i64, _i64, _vp], _int),
+    "leafq_argmax": ([_vp, _vp, _i64, _i64, _vp], _int),
+    "leafq_expf": ([_vp, _vp, _i64, _vp], _int),
+    "leafq_advance_position": ([_vp, _vp, ctypes.c_int32], _int),
 }
 
 

@@ -1,0 +1,523 @@
+// The decoder's non-linear operators around the quantised linears
+// (Decoder::Impl::forward_into, decoder.cpp:1282-1452), on the GPU.
+//
+//   embed_kernel          embedding rows Weight::value(id, col) * embedding_scale
+//                         (decoder.cpp:1293-1304, :241-250)
+//   rmsnorm_kernel        optional residual add, then RMSNorm (norm(),
+//                         decoder.cpp:706-727) with the reference's epilogue
+//                         order (x * scale) * weight + 0
+//   rotary_append_kernel  RoPE on q and k from host-computed tables
+//                         (decoder.cpp:1234-1281), q to head-major order, k and
+//                         v appended to the per-layer cache (kv_cache.cpp:21-59)
+//   attention_kernel      causal GQA attention (KVCache::attend ->
+//                         transformer.cpp:93-145): q.k, scaled twice, softmax,
+//                         probability-weighted V
+//   silu_gate_kernel      up * (gate / (1 + expf(-gate))) (decoder.cpp:982-988)
+//   argmax_kernel         first index of the largest logit
+//                         (main_decoder.cpp:101, std::max_element)
+//
+// Every result is bit-identical to the reference decoder's (built as
+// leaf/cli.py:66 builds it, on Linux):
+// * sums run in the reference's order: RMSNorm's sum of squares, the
+//   attention dot product (transformer.cpp is built without -mavx2, so
+//   fast_dot is the sequential scalar_dot), the softmax denominator and each
+//   output element's probability-weighted sum over keys are sequential;
+// * the exponential is libm's expf (attention transformer.cpp:130, SiLU
+//   decoder.cpp:983; the vector SiLU kernel is enabled on Windows builds
+//   only, decoder_config.h:5-11).  expf_libm restates the algorithm of the
+//   system libm (GNU C Library 2.39 expf, from Arm's optimized-routines):
+//   k = round(x * 32 / ln 2), r = x * 32 / ln 2 - k, 2^(k/32) from a
+//   32-entry table of 2^(i/32), a cubic in r, all in double, one rounding
+//   to float.  The table is computed on the host (2^(i/32) rounded to
+//   double) and passed as a kernel parameter.  The restatement was checked
+//   against libm expf on all 2^32 float inputs.
+// Sequential sums cost latency (a 2048-element sum of squares is a chain of
+// 2048 dependent additions); they are the price of identical greedy tokens:
+// the random-init decoders amplify a last-bit difference anywhere into
+// different logits within a few layers.
+#include <cmath>
+#include <cstring>
+
+#include "leafq_device.cuh"
+#include "leafq_internal.h"
+
+namespace leafq {
+namespace {
+
+struct ExpTable {
+    unsigned long long bits[32];
+};
+
+constexpr int kNormThreads = 256;
+constexpr int kAttnThreads = 128;
+constexpr int kArgmaxThreads = 1024;
+
+// expf of the system libm (see the file comment).  tab.bits[i] = bits of
+// 2^(i/32) rounded to double, minus i << 47.
+__device__ __forceinline__ float expf_libm(float x, const ExpTable& tab) {
+    const uint32_t ux = __float_as_uint(x);
+    const uint32_t abstop = (ux >> 20) & 0x7ffu;
+    if (abstop >= 0x42bu) {  // |x| >= 88 (top 12 bits of 88.0f), inf, nan
+        if (ux == 0xff800000u) return 0.0f;
+        if (abstop >= 0x7f8u) return __fadd_rn(x, x);
+        if (x > 0x1.62e42ep6f) return __int_as_float(0x7f800000);
+        if (x < -0x1.9fe368p6f) return 0.0f;
+    }
+    const double inv_ln2_n = 0x1.71547652b82fep+0 * 32.0;
+    const double shift = 0x1.8p+52;
+    const double xd = static_cast<double>(x);
+    double kd = __fma_rn(inv_ln2_n, xd, shift);
+    const unsigned long long ki = static_cast<unsigned long long>(__double_as_longlong(kd));
+    kd = __dsub_rn(kd, shift);
+    const double r = __fma_rn(inv_ln2_n, xd, -kd);
+    unsigned long long t = tab.bits[ki % 32];
+    t += ki << 47;
+    const double sc = __longlong_as_double(static_cast<long long>(t));
+    const double c0 = 0x1.c6af84b912394p-5 / 32.0 / 32.0 / 32.0;
+    const double c1 = 0x1.ebfce50fac4f3p-3 / 32.0 / 32.0;
+    const double c2 = 0x1.62e42ff0c52d6p-1 / 32.0;
+    const double z = __fma_rn(c0, r, c1);
+    const double r2 = __dmul_rn(r, r);
+    double y = __fma_rn(c2, r, 1.0);
+    y = __fma_rn(z, r2, y);
+    y = __dmul_rn(y, sc);
+    return __double2float_rn(y);
+}
+
+__device__ __forceinline__ float block_max(float v, float* scratch) {
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();
+    if (lane == 0) scratch[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+        v = lane < static_cast<int>(blockDim.x >> 5) ? scratch[lane] : -INFINITY;
+        for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+        if (lane == 0) scratch[32] = v;
+    }
+    __syncthreads();
+    return scratch[32];
+}
+
+// ------------------------------------------------------------------ embed
+__global__ void embed_kernel(const int32_t* __restrict__ ids, const void* __restrict__ table,
+                             const float* __restrict__ scales, int bits, int64_t group, int64_t vocab,
+                             int64_t hidden, float embedding_scale, float* __restrict__ out,
+                             int32_t* __restrict__ error_flag) {
+    const int64_t t = blockIdx.x;
+    int64_t id = ids[t];
+    if (id < 0 || id >= vocab) {
+        if (threadIdx.x == 0 && error_flag) atomicExch(error_flag, 1);
+        id = 0;
+    }
+    for (int64_t c = threadIdx.x; c < hidden; c += blockDim.x) {
+        const int64_t index = id * hidden + c;
+        float v;
+        if (bits == 32) {
+            v = static_cast<const float*>(table)[index];
+        } else {
+            int q;
+            if (bits == 8) {
+                q = static_cast<const int8_t*>(table)[index];
+            } else {
+                q = (static_cast<const uint8_t*>(table)[index / 2] >> ((index % 2) * 4)) & 15;
+                if (q >= 8) q -= 16;
+            }
+            v = __fmul_rn(static_cast<float>(q), scales[id * (hidden / group) + c / group]);
+        }
+        out[t * hidden + c] = __fmul_rn(v, embedding_scale);
+    }
+}
+
+// ---------------------------------------------------------------- rmsnorm
+// hidden[t] (+)= delta[t] (+ 0 when add_zero), written back; then
+// out[t] = (hidden * (1 / sqrt(sum(h^2) / width + eps))) * weight + 0, the
+// sum of squares accumulated left to right as norm() does.
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(
+    float* __restrict__ hidden, const float* __restrict__ delta, int add_zero, int64_t width,
+    const float* __restrict__ weight, float epsilon, float* __restrict__ out) {
+    extern __shared__ float row[];  // [width] values, then [width] squares
+    float* squares = row + width;
+    __shared__ float total;
+    const int64_t t = blockIdx.x;
+    float* h = hidden + t * width;
+    for (int64_t c = threadIdx.x; c < width; c += blockDim.x) {
+        float v = h[c];
+        if (delta) {
+            float d = delta[t * width + c];
+            if (add_zero) d = __fadd_rn(d, 0.0f);
+            v = __fadd_rn(v, d);
+            h[c] = v;
+        }
+        row[c] = v;
+        squares[c] = __fmul_rn(v, v);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float sq = 0.0f;
+        int64_t c = 0;
+        if ((width & 3) == 0)
+            for (; c + 4 <= width; c += 4) {
+                const float4 q = *reinterpret_cast<const float4*>(squares + c);
+                sq = __fadd_rn(sq, q.x);
+                sq = __fadd_rn(sq, q.y);
+                sq = __fadd_rn(sq, q.z);
+                sq = __fadd_rn(sq, q.w);
+            }
+        for (; c < width; ++c) sq = __fadd_rn(sq, squares[c]);
+        total = sq;
+    }
+    __syncthreads();
+    const float scale =
+        __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(width)), epsilon)));
+    for (int64_t c = threadIdx.x; c < width; c += blockDim.x)
+        out[t * width + c] = __fadd_rn(__fmul_rn(__fmul_rn(row[c], scale), weight[c]), 0.0f);
+}
+
+// ------------------------------------------------------ rotary + KV append
+// qkv[t] = [q (heads*dim) | k (kv*dim) | v (kv*dim)].  Block (t, head):
+// heads first (q -> q_heads[head][t]), then kv heads (k -> k cache, v -> v cache).
+__global__ void rotary_append_kernel(const float* __restrict__ qkv, int64_t tokens, int heads,
+                                     int kv_heads, int dim, int rotary_dim,
+                                     const float* __restrict__ cos_table,
+                                     const float* __restrict__ sin_table,
+                                     const int32_t* __restrict__ position,
+                                     float* __restrict__ q_heads, float* __restrict__ k_cache,
+                                     float* __restrict__ v_cache, int64_t capacity) {
+    const int64_t t = blockIdx.x;
+    const int head = blockIdx.y;
+    const int64_t width = (int64_t)(heads + 2 * kv_heads) * dim;
+    const int64_t pos = static_cast<int64_t>(*position) + t;
+    const int half = rotary_dim / 2;
+    const float* row = qkv + t * width;
+    const float* src;
+    float* dst;
+    if (head < heads) {
+        src = row + (int64_t)head * dim;
+        dst = q_heads + ((int64_t)head * tokens + t) * dim;
+    } else {
+        const int kvh = head - heads;
+        src = row + (int64_t)heads * dim + (int64_t)kvh * dim;
+        dst = k_cache + ((int64_t)kvh * capacity + pos) * dim;
+        const float* vsrc = row + (int64_t)(heads + kv_heads) * dim + (int64_t)kvh * dim;
+        float* vdst = v_cache + ((int64_t)kvh * capacity + pos) * dim;
+        for (int i = threadIdx.x; i < dim; i += blockDim.x) vdst[i] = vsrc[i];
+    }
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) {
+        if (i < half) {
+            const float c = cos_table[pos * half + i], s = sin_table[pos * half + i];
+            const float a = src[i], b = src[i + half];
+            dst[i] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+            dst[i + half] = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
+        } else if (i >= rotary_dim) {
+            dst[i] = src[i];
+        }
+    }
+}
+
+// -------------------------------------------------------------- attention
+// Block (head, t): query t of this chunk attends keys [0, position + t]
+// (attention_impl, transformer.cpp:93-145).  out[t][head*dim + d].
+// Shared memory: q [dim], then scores [capacity].
+__global__ void __launch_bounds__(kAttnThreads) attention_kernel(
+    const float* __restrict__ q_heads, const float* __restrict__ k_cache,
+    const float* __restrict__ v_cache, int64_t tokens, int heads, int kv_heads, int dim,
+    const int32_t* __restrict__ position, int64_t capacity, float scale, float* __restrict__ out,
+    const __grid_constant__ ExpTable tab) {
+    extern __shared__ float smem[];
+    float* q = smem;
+    float* scores = smem + dim;
+    __shared__ float scratch[33];
+    __shared__ float denominator_s;
+    const int head = blockIdx.x;
+    const int64_t t = blockIdx.y;
+    const int kvh = head / (heads / kv_heads);
+    const int64_t keys = static_cast<int64_t>(*position) + t + 1;
+    const float* qrow = q_heads + ((int64_t)head * tokens + t) * dim;
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) q[i] = qrow[i];
+    __syncthreads();
+    const float* kbase = k_cache + (int64_t)kvh * capacity * dim;
+    const float* vbase = v_cache + (int64_t)kvh * capacity * dim;
+    // scores[k] = dot(q, k) * scale * scale, the dot summed left to right.
+    float local_max = -INFINITY;
+    for (int64_t k = threadIdx.x; k < keys; k += blockDim.x) {
+        const float* krow = kbase + k * dim;
+        float dot = 0.0f;
+        for (int d = 0; d < dim; ++d) dot = __fadd_rn(dot, __fmul_rn(q[d], krow[d]));
+        const float s = __fmul_rn(__fmul_rn(dot, scale), scale);
+        scores[k] = s;
+        local_max = fmaxf(local_max, s);
+    }
+    const float maximum = block_max(local_max, scratch);
+    for (int64_t k = threadIdx.x; k < keys; k += blockDim.x)
+        scores[k] = expf_libm(__fsub_rn(scores[k], maximum), tab);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float den = 0.0f;
+        for (int64_t k = 0; k < keys; ++k) den = __fadd_rn(den, scores[k]);
+        denominator_s = den;
+    }
+    __syncthreads();
+    const float denominator = denominator_s;
+    for (int64_t k = threadIdx.x; k < keys; k += blockDim.x) scores[k] = __fdiv_rn(scores[k], denominator);
+    __syncthreads();
+    // out[d] = sum over keys, in order, of probability * value (thread per d).
+    for (int d = threadIdx.x; d < dim; d += blockDim.x) {
+        float acc = 0.0f;
+        for (int64_t k = 0; k < keys; ++k) acc = __fadd_rn(acc, __fmul_rn(scores[k], vbase[k * dim + d]));
+        out[(t * heads + head) * (int64_t)dim + d] = acc;
+    }
+}
+
+// -------------------------------------------------------------- silu gate
+// gate_up[t] = [gate (width) | up (width)]; out[t][j] = up * (g / (1 + expf(-g))).
+__global__ void silu_gate_kernel(const float* __restrict__ gate_up, int64_t tokens, int64_t width,
+                                 float* __restrict__ out, const __grid_constant__ ExpTable tab) {
+    const int64_t n = tokens * width;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t t = i / width, j = i - t * width;
+        const float g = gate_up[t * 2 * width + j];
+        const float u = gate_up[t * 2 * width + width + j];
+        out[i] = __fmul_rn(u, __fdiv_rn(g, __fadd_rn(1.0f, expf_libm(-g, tab))));
+    }
+}
+
+// ----------------------------------------------------------------- argmax
+__global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* __restrict__ logits,
+                                                                 int64_t width,
+                                                                 int32_t* __restrict__ ids) {
+    __shared__ float best_v[kArgmaxThreads / 32];
+    __shared__ int best_i[kArgmaxThreads / 32];
+    const float* row = logits + (int64_t)blockIdx.x * width;
+    float v = -INFINITY;
+    int idx = 0x7fffffff;
+    for (int64_t c = threadIdx.x; c < width; c += blockDim.x) {
+        const float x = row[c];
+        if (x > v || idx == 0x7fffffff) {
+            v = x;
+            idx = static_cast<int>(c);
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+        if (ov > v || (ov == v && oi < idx)) {
+            v = ov;
+            idx = oi;
+        }
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        best_v[warp] = v;
+        best_i[warp] = idx;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float bv = best_v[0];
+        int bi = best_i[0];
+        for (int w = 1; w < kArgmaxThreads / 32; ++w)
+            if (best_v[w] > bv || (best_v[w] == bv && best_i[w] < bi)) {
+                bv = best_v[w];
+                bi = best_i[w];
+            }
+        ids[blockIdx.x] = bi;
+    }
+}
+
+__global__ void advance_kernel(int32_t* position, int32_t count) { *position += count; }
+
+__global__ void expf_kernel(const float* __restrict__ x, int64_t n, float* __restrict__ y,
+                            const __grid_constant__ ExpTable tab) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x)
+        y[i] = expf_libm(x[i], tab);
+}
+
+// 2^(i/32) rounded to double, minus i << 47 (the table of expf_libm).
+const ExpTable& exp_table() {
+    static const ExpTable table = [] {
+        ExpTable t;
+        for (int i = 0; i < 32; ++i) {
+            const double v = static_cast<double>(std::exp2(static_cast<long double>(i) / 32.0L));
+            unsigned long long bits;
+            std::memcpy(&bits, &v, sizeof(bits));
+            t.bits[i] = bits - (static_cast<unsigned long long>(i) << 47);
+        }
+        return t;
+    }();
+    return table;
+}
+
+}  // namespace
+}  // namespace leafq
+
+using namespace leafq;
+
+extern "C" {
+
+int leafq_embed(void* stream, const int32_t* ids, int64_t tokens, const void* table,
+                const float* scales, int bits, int64_t group, int64_t vocab, int64_t hidden,
+                float embedding_scale, float* out, int32_t* error_flag) {
+    clear_error();
+    if (tokens < 0 || vocab <= 0 || hidden <= 0 || (bits != 32 && bits != 8 && bits != 4) ||
+        (bits != 32 && (group <= 0 || hidden % group != 0 || !scales)) ||
+        (bits == 4 && hidden % 2 != 0)) {
+        set_error("leafq_embed: invalid arguments");
+        return LEAFQ_ERR_INVALID;
+    }
+    if (tokens == 0) return LEAFQ_OK;
+    if (!ids || !table || !out || tokens > 0x7fffffff) {
+        set_error("leafq_embed: null pointer or too many tokens");
+        return LEAFQ_ERR_INVALID;
+    }
+    return launch(embed_kernel, dim3(static_cast<unsigned>(tokens)), dim3(256), 0,
+                  static_cast<cudaStream_t>(stream), false, "embed", ids, table, scales, bits, group,
+                  vocab, hidden, embedding_scale, out, error_flag);
+}
+
+int leafq_rmsnorm(void* stream, float* hidden, const float* delta, int add_zero, int64_t tokens,
+                  int64_t width, const float* weight, float epsilon, float* out) {
+    clear_error();
+    if (tokens < 0 || width <= 0 || width > 16384 || tokens > 0x7fffffff) {
+        set_error("leafq_rmsnorm: width must be 1..16384");
+        return LEAFQ_ERR_INVALID;
+    }
+    if (tokens == 0) return LEAFQ_OK;
+    if (!hidden || !weight || !out) {
+        set_error("leafq_rmsnorm: null pointer");
+        return LEAFQ_ERR_INVALID;
+    }
+    const size_t smem = 2 * static_cast<size_t>(width) * sizeof(float);
+    int st = allow_smem(reinterpret_cast<const void*>(rmsnorm_kernel), smem, "rmsnorm");
+    if (st) return st;
+    return launch(rmsnorm_kernel, dim3(static_cast<unsigned>(tokens)), dim3(kNormThreads), smem,
+                  static_cast<cudaStream_t>(stream), false, "rmsnorm", hidden, delta, add_zero, width,
+                  weight, epsilon, out);
+}
+
+int leafq_rope_tables(float theta, int rotary_dim, int64_t positions, float* cos_out,
+                      float* sin_out) {
+    clear_error();
+    if (!(theta > 0.0f) || rotary_dim <= 0 || rotary_dim % 2 || positions < 0 || !cos_out || !sin_out) {
+        set_error("leafq_rope_tables: invalid arguments");
+        return LEAFQ_ERR_INVALID;
+    }
+    // decoder.cpp:929-933 and :1248-1256, with the same float libm calls.
+    const int half = rotary_dim / 2;
+    for (int i = 0; i < half; ++i) {
+        const float frequency =
+            1.0f / std::pow(theta, static_cast<float>(2 * i) / static_cast<float>(rotary_dim));
+        for (int64_t p = 0; p < positions; ++p) {
+            const float angle = static_cast<float>(p) * frequency;
+            cos_out[p * half + i] = std::cos(angle);
+            sin_out[p * half + i] = std::sin(angle);
+        }
+    }
+    return LEAFQ_OK;
+}
+
+int leafq_rotary_append(void* stream, const float* qkv, int64_t tokens, int heads, int kv_heads,
+                        int dim, int rotary_dim, const float* cos_table, const float* sin_table,
+                        const int32_t* position, float* q_heads, float* k_cache, float* v_cache,
+                        int64_t capacity) {
+    clear_error();
+    if (tokens < 0 || heads <= 0 || kv_heads <= 0 || heads % kv_heads || dim <= 0 ||
+        rotary_dim < 0 || rotary_dim > dim || rotary_dim % 2 || capacity <= 0 || tokens > 65535) {
+        set_error("leafq_rotary_append: invalid arguments");
+        return LEAFQ_ERR_INVALID;
+    }
+    if (tokens == 0) return LEAFQ_OK;
+    if (!qkv || !position || !q_heads || !k_cache || !v_cache || (rotary_dim && (!cos_table || !sin_table))) {
+        set_error("leafq_rotary_append: null pointer");
+        return LEAFQ_ERR_INVALID;
+    }
+    const int threads = dim < 128 ? ((dim + 31) / 32) * 32 : 128;
+    return launch(rotary_append_kernel, dim3(static_cast<unsigned>(tokens), heads + kv_heads),
+                  dim3(threads), 0, static_cast<cudaStream_t>(stream), false, "rotary_append", qkv,
+                  tokens, heads, kv_heads, dim, rotary_dim, cos_table, sin_table, position, q_heads,
+                  k_cache, v_cache, capacity);
+}
+
+int leafq_attention(void* stream, const float* q_heads, const float* k_cache, const float* v_cache,
+                    int64_t tokens, int heads, int kv_heads, int dim, const int32_t* position,
+                    int64_t capacity, float scale, float* out) {
+    clear_error();
+    if (tokens < 0 || heads <= 0 || kv_heads <= 0 || heads % kv_heads || dim <= 0 || dim > 1024 ||
+        capacity <= 0 || tokens > 65535 || !(scale > 0.0f)) {
+        set_error("leafq_attention: invalid arguments");
+        return LEAFQ_ERR_INVALID;
+    }
+    if (tokens == 0) return LEAFQ_OK;
+    if (!q_heads || !k_cache || !v_cache || !position || !out) {
+        set_error("leafq_attention: null pointer");
+        return LEAFQ_ERR_INVALID;
+    }
+    const size_t smem = (static_cast<size_t>(dim) + capacity) * sizeof(float);
+    if (smem > static_cast<size_t>(max_smem_per_block())) {
+        set_error("leafq_attention: context capacity exceeds shared memory");
+        return LEAFQ_ERR_UNSUPPORTED;
+    }
+    int st = allow_smem(reinterpret_cast<const void*>(attention_kernel), smem, "attention");
+    if (st) return st;
+    return launch(attention_kernel, dim3(heads, static_cast<unsigned>(tokens)), dim3(kAttnThreads),
+                  smem, static_cast<cudaStream_t>(stream), false, "attention", q_heads, k_cache,
+                  v_cache, tokens, heads, kv_heads, dim, position, capacity, scale, out, exp_table());
+}
+
+int leafq_silu_gate(void* stream, const float* gate_up, int64_t tokens, int64_t width, float* out) {
+    clear_error();
+    if (tokens < 0 || width <= 0) {
+        set_error("leafq_silu_gate: invalid arguments");
+        return LEAFQ_ERR_INVALID;
+    }
+    if (tokens == 0) return LEAFQ_OK;
+    if (!gate_up || !out) {
+        set_error("leafq_silu_gate: null pointer");
+        return LEAFQ_ERR_INVALID;
+    }
+    const int64_t n = tokens * width;
+    const int64_t blocks = std::min<int64_t>((n + 255) / 256, static_cast<int64_t>(sm_count()) * 8);
+    return launch(silu_gate_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0,
+                  static_cast<cudaStream_t>(stream), false, "silu_gate", gate_up, tokens, width, out,
+                  exp_table());
+}
+
+int leafq_argmax(void* stream, const float* logits, int64_t rows, int64_t width, int32_t* ids) {
+    clear_error();
+    if (rows < 0 || width <= 0 || width > 0x7fffffff || rows > 0x7fffffff) {
+        set_error("leafq_argmax: invalid arguments");
+        return LEAFQ_ERR_INVALID;
+    }
+    if (rows == 0) return LEAFQ_OK;
+    if (!logits || !ids) {
+        set_error("leafq_argmax: null pointer");
+        return LEAFQ_ERR_INVALID;
+    }
+    return launch(argmax_kernel, dim3(static_cast<unsigned>(rows)), dim3(kArgmaxThreads), 0,
+                  static_cast<cudaStream_t>(stream), false, "argmax", logits, width, ids);
+}
+
+int leafq_expf(void* stream, const float* x, int64_t n, float* y) {
+    clear_error();
+    if (n < 0 || (n > 0 && (!x || !y))) {
+        set_error("leafq_expf: invalid arguments");
+        return LEAFQ_ERR_INVALID;
+    }
+    if (n == 0) return LEAFQ_OK;
+    const int64_t blocks = std::min<int64_t>((n + 255) / 256, static_cast<int64_t>(sm_count()) * 16);
+    return launch(expf_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0,
+                  static_cast<cudaStream_t>(stream), false, "expf", x, n, y, exp_table());
+}
+
+int leafq_advance_position(void* stream, int32_t* position, int32_t count) {
+    clear_error();
+    if (!position || count < 0) {
+        set_error("leafq_advance_position: invalid arguments");
+        return LEAFQ_ERR_INVALID;
+    }
+    return launch(advance_kernel, dim3(1), dim3(1), 0, static_cast<cudaStream_t>(stream), false,
+                  "advance_position", position, count);
+}
+
+}  // extern "C"

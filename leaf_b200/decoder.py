@@ -1,0 +1,277 @@
+"""GPU port of Leaf's decoder (``leaf::runtime::Decoder``, decoder.h) for
+Llama-family artifacts with quantised linears.
+
+``Decoder(artifact).forward(ids)`` follows ``Impl::forward_into``
+(decoder.cpp:1282-1452) op for op: embedding, per layer RMSNorm -> q|k|v ->
+RoPE + KV append -> attention -> o -> residual + RMSNorm -> gate|up -> SiLU
+gate -> down -> residual (+ next RMSNorm), final RMSNorm, lm_head on the last
+row.  Every linear is ``leafq_linear`` (W8A8 / W4A8 with activation_bits 8,
+weight-only with 32); the other operators are the library's decoder kernels.
+q, k and v (and gate and up) run as one linear over their concatenated rows
+-- rows are independent, so the outputs are bit-identical to the separate
+calls the reference makes.  ``generate`` is the greedy loop of
+main_decoder.cpp:95-113: one prefill forward, then one CUDA-graph replay per
+token with the argmax, the next embedding and the position update on the
+device (no host round trip per token).
+
+Supported artifacts: RMSNorm, RoPE, gated SiLU, sequential residual, no
+sliding window, no Q/K norm (the Llama / Mistral-without-window / Qwen2
+family); anything else raises.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import LeafError, check, load
+from .artifact import Artifact, HostTensor
+from .linear import QuantWeight, Workspace
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _concat_rows(parts: list[HostTensor]) -> tuple:
+    bits, group, cols = parts[0].bits, parts[0].group, parts[0].cols
+    if any(p.bits != bits or p.group != group or p.cols != cols for p in parts):
+        raise LeafError(_lib.LEAFQ_ERR_UNSUPPORTED, "fused projections need one precision and group")
+    data = np.concatenate([np.asarray(p.data) for p in parts], axis=0)
+    scales = None if bits == 32 else np.concatenate([np.asarray(p.scales) for p in parts], axis=0)
+    return data, scales, sum(p.rows for p in parts), cols, bits, group
+
+
+class Decoder:
+    def __init__(self, artifact, activation_bits: int = 8, device="cuda",
+                 capacity: Optional[int] = None):
+        art = artifact if isinstance(artifact, Artifact) else Artifact(artifact)
+        cfg = art.config
+        if not (cfg.norm_kind == 0 and cfg.position_kind == 0 and cfg.gated == 1 and
+                cfg.activation == 0 and cfg.parallel == 0 and cfg.sliding_window == 0 and
+                not cfg.qk_norm and not cfg.rope_frequencies and cfg.position_offset == 0):
+            raise LeafError(_lib.LEAFQ_ERR_UNSUPPORTED,
+                            "GPU decoder supports RMSNorm / RoPE / gated SiLU decoders without "
+                            "sliding window or Q/K norm")
+        if activation_bits not in (8, 32):
+            raise LeafError(_lib.LEAFQ_ERR_INVALID, "activation bits must be 8 or 32")
+        self.cfg = cfg
+        self.activation_bits = activation_bits
+        self.device = torch.device(device)
+        self.capacity = int(capacity or cfg.max_positions)
+        self.lib = load()
+        dev = self.device
+
+        def f32(t: HostTensor):
+            return torch.from_numpy(np.array(t.data, dtype=np.float32).reshape(-1)).to(dev)
+
+        def weight(parts):
+            data, scales, rows, cols, bits, group = _concat_rows(parts)
+            w = QuantWeight.from_host(data, scales, rows, cols, bits, group, device=dev)
+            w.check()
+            return w
+
+        emb = art.get("model.embed_tokens.weight")
+        self.embed_table = torch.from_numpy(np.array(emb.data)).to(dev)
+        self.embed_scales = (None if emb.scales is None else
+                             torch.from_numpy(np.array(emb.scales)).to(dev))
+        self.embed_bits, self.embed_group = emb.bits, emb.group
+        self.layers = []
+        for i in range(cfg.layers):
+            p = f"model.layers.{i}."
+            get = art.get
+            self.layers.append(dict(
+                input_norm=f32(get(p + "input_layernorm.weight")),
+                post_norm=f32(get(p + "post_attention_layernorm.weight")),
+                qkv=weight([get(p + "self_attn.q_proj.weight"), get(p + "self_attn.k_proj.weight"),
+                            get(p + "self_attn.v_proj.weight")]),
+                o=weight([get(p + "self_attn.o_proj.weight")]),
+                gate_up=weight([get(p + "mlp.gate_proj.weight"), get(p + "mlp.up_proj.weight")]),
+                down=weight([get(p + "mlp.down_proj.weight")]),
+            ))
+            for name in ("q", "k", "v", "o"):
+                if get(p + f"self_attn.{name}_proj.bias") is not None:
+                    raise LeafError(_lib.LEAFQ_ERR_UNSUPPORTED, "projection biases are not supported")
+        self.final_norm = f32(art.get("model.norm.weight")) if cfg.final_norm else None
+        self.lm_head = weight([art.get("lm_head.weight")])
+        d, kv = cfg.head_dim, cfg.kv_heads
+        self.k_cache = [torch.zeros((kv, self.capacity, d), dtype=torch.float32, device=dev)
+                        for _ in range(cfg.layers)]
+        self.v_cache = [torch.zeros_like(k) for k in self.k_cache]
+        half = cfg.rotary_dim // 2
+        cos = np.empty((self.capacity, half), dtype=np.float32)
+        sin = np.empty_like(cos)
+        check(self.lib.leafq_rope_tables(ctypes.c_float(cfg.theta), cfg.rotary_dim, self.capacity,
+                                         cos.ctypes.data, sin.ctypes.data))
+        self.cos = torch.from_numpy(cos).to(dev)
+        self.sin = torch.from_numpy(sin).to(dev)
+        # decoder.cpp:1348: both q and k are scaled by 1/sqrt(sqrt(dim)).
+        self.scale = float(np.float32(1.0) / np.sqrt(np.sqrt(np.float32(d))))
+        self.position = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.error_flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.length = 0
+        self._buffers: dict[int, dict] = {}
+        self.graph: Optional[torch.cuda.CUDAGraph] = None
+
+    # ------------------------------------------------------------ buffers
+    def _bufs(self, tokens: int) -> dict:
+        b = self._buffers.get(tokens)
+        if b is None:
+            c = self.cfg
+            q = c.heads * c.head_dim
+            dev = self.device
+            e = lambda *s: torch.empty(s, dtype=torch.float32, device=dev)  # noqa: E731
+            b = dict(ids=torch.zeros(tokens, dtype=torch.int32, device=dev), hidden=e(tokens, c.hidden),
+                     normalized=e(tokens, c.hidden), qkv=e(tokens, q + 2 * c.kv_heads * c.head_dim),
+                     q_heads=e(c.heads, tokens, c.head_dim), attn=e(tokens, q), o=e(tokens, c.hidden),
+                     gate_up=e(tokens, 2 * c.intermediate), act=e(tokens, c.intermediate),
+                     down=e(tokens, c.hidden), logits=e(1, c.vocab), workspace=Workspace(dev))
+            # Each chunk size owns its workspace, sized once: a captured graph
+            # keeps its pointers, so nothing it uses may be reallocated.
+            for w in self._weights():
+                for rows in (tokens, 1):
+                    need = self.lib.leafq_linear_workspace_bytes(rows, w.cols, w.bits, w.group,
+                                                                 self.activation_bits)
+                    if need:
+                        b["workspace"].get(need)
+            self._buffers[tokens] = b
+        return b
+
+    def _weights(self):
+        for layer in self.layers:
+            yield from (layer["qkv"], layer["o"], layer["gate_up"], layer["down"])
+        yield self.lm_head
+
+    # -------------------------------------------------------------- ops
+    def _linear(self, x: torch.Tensor, w: QuantWeight, out: torch.Tensor, tokens: int,
+                workspace: Workspace) -> None:
+        lib = self.lib
+        need = lib.leafq_linear_workspace_bytes(tokens, w.cols, w.bits, w.group, self.activation_bits)
+        ws = workspace.buffer if need else None
+        if ws is not None and ws.numel() < need:
+            raise LeafError(_lib.LEAFQ_ERR_INVALID, "decoder workspace too small")
+        check(lib.leafq_linear(_stream(), x.data_ptr(), tokens, w.cols, w.data.data_ptr(),
+                               None if w.scales is None else w.scales.data_ptr(), w.rows, w.bits,
+                               w.group, self.activation_bits, None, out.data_ptr(),
+                               None if ws is None else ws.data_ptr(), 0 if ws is None else ws.numel(),
+                               0))
+
+    def _forward_device(self, b: dict, tokens: int) -> None:
+        """One forward of `tokens` ids already in b["ids"] at the device
+        position; logits of the last row in b["logits"]; position advanced."""
+        c, lib, s = self.cfg, self.lib, _stream()
+        check(lib.leafq_embed(s, b["ids"].data_ptr(), tokens, self.embed_table.data_ptr(),
+                              None if self.embed_scales is None else self.embed_scales.data_ptr(),
+                              self.embed_bits, self.embed_group, c.vocab, c.hidden,
+                              ctypes.c_float(c.embedding_scale), b["hidden"].data_ptr(),
+                              self.error_flag.data_ptr()))
+        check(lib.leafq_rmsnorm(s, b["hidden"].data_ptr(), None, 0, tokens, c.hidden,
+                                self.layers[0]["input_norm"].data_ptr(), ctypes.c_float(c.epsilon),
+                                b["normalized"].data_ptr()))
+        for i, layer in enumerate(self.layers):
+            self._linear(b["normalized"], layer["qkv"], b["qkv"], tokens, b["workspace"])
+            check(lib.leafq_rotary_append(s, b["qkv"].data_ptr(), tokens, c.heads, c.kv_heads,
+                                          c.head_dim, c.rotary_dim, self.cos.data_ptr(),
+                                          self.sin.data_ptr(), self.position.data_ptr(),
+                                          b["q_heads"].data_ptr(), self.k_cache[i].data_ptr(),
+                                          self.v_cache[i].data_ptr(), self.capacity))
+            check(lib.leafq_attention(s, b["q_heads"].data_ptr(), self.k_cache[i].data_ptr(),
+                                      self.v_cache[i].data_ptr(), tokens, c.heads, c.kv_heads,
+                                      c.head_dim, self.position.data_ptr(), self.capacity,
+                                      ctypes.c_float(self.scale), b["attn"].data_ptr()))
+            self._linear(b["attn"], layer["o"], b["o"], tokens, b["workspace"])
+            check(lib.leafq_rmsnorm(s, b["hidden"].data_ptr(), b["o"].data_ptr(), 0, tokens, c.hidden,
+                                    layer["post_norm"].data_ptr(), ctypes.c_float(c.epsilon),
+                                    b["normalized"].data_ptr()))
+            self._linear(b["normalized"], layer["gate_up"], b["gate_up"], tokens, b["workspace"])
+            check(lib.leafq_silu_gate(s, b["gate_up"].data_ptr(), tokens, c.intermediate,
+                                      b["act"].data_ptr()))
+            self._linear(b["act"], layer["down"], b["down"], tokens, b["workspace"])
+            last = i + 1 == len(self.layers)
+            norm = (self.layers[i + 1]["input_norm"] if not last else self.final_norm)
+            if norm is not None:
+                check(lib.leafq_rmsnorm(s, b["hidden"].data_ptr(), b["down"].data_ptr(), 1, tokens,
+                                        c.hidden, norm.data_ptr(), ctypes.c_float(c.epsilon),
+                                        b["normalized"].data_ptr()))
+            else:  # no final norm: the logits read the residual stream itself
+                raise LeafError(_lib.LEAFQ_ERR_UNSUPPORTED, "artifacts without a final norm")
+        last_row = b["normalized"][tokens - 1:tokens]
+        self._linear(last_row, self.lm_head, b["logits"], 1, b["workspace"])
+        check(lib.leafq_advance_position(s, self.position.data_ptr(), tokens))
+
+    # ----------------------------------------------------------- public API
+    def reset(self) -> None:
+        """Decoder::reset: empty every KV cache."""
+        self.length = 0
+        self.position.zero_()
+
+    def forward(self, ids) -> torch.Tensor:
+        """Decoder::forward_into(ids, logits) with all_logits = false: the
+        last position's logits [1, vocab] (a device tensor reused by later
+        calls)."""
+        ids = [int(i) for i in ids]
+        if not ids:
+            raise LeafError(_lib.LEAFQ_ERR_INVALID, "input tokens are empty")
+        if self.length + len(ids) > min(self.cfg.max_positions, self.capacity):
+            raise LeafError(_lib.LEAFQ_ERR_INVALID, "context length exceeds artifact limit")
+        if any(i < 0 or i >= self.cfg.vocab for i in ids):
+            raise LeafError(_lib.LEAFQ_ERR_INVALID, "token id exceeds vocabulary")
+        b = self._bufs(len(ids))
+        b["ids"].copy_(torch.tensor(ids, dtype=torch.int32))
+        self._forward_device(b, len(ids))
+        self.length += len(ids)
+        return b["logits"]
+
+    def capture_decode(self) -> None:
+        """Capture one decode step (ids from the previous step's argmax) as
+        a CUDA graph."""
+        b = self._bufs(1)
+        stream = torch.cuda.Stream(self.device)
+        stream.wait_stream(torch.cuda.current_stream(self.device))
+        saved = self.position.clone()
+        with torch.cuda.stream(stream):
+            self._forward_device(b, 1)  # warm-up outside capture (lazy loads, smem attributes)
+            check(self.lib.leafq_argmax(_stream(), b["logits"].data_ptr(), 1, self.cfg.vocab,
+                                        b["ids"].data_ptr()))
+        torch.cuda.current_stream(self.device).wait_stream(stream)
+        torch.cuda.synchronize(self.device)
+        self.position.copy_(saved)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            self._forward_device(b, 1)
+            check(self.lib.leafq_argmax(_stream(), b["logits"].data_ptr(), 1, self.cfg.vocab,
+                                        b["ids"].data_ptr()))
+        self.graph = graph
+
+    def generate(self, prompt, max_new: int) -> list[int]:
+        """main_decoder.cpp:95-113 greedy continuation without EOS handling
+        on the device: prefill, then one graph replay per further token."""
+        if self.graph is None:
+            self.capture_decode()
+        if self.length + len(prompt) + max_new - 1 > min(self.cfg.max_positions, self.capacity):
+            raise LeafError(_lib.LEAFQ_ERR_INVALID, "context length exceeds artifact limit")
+        logits = self.forward(prompt)
+        step = self._bufs(1)
+        check(self.lib.leafq_argmax(_stream(), logits.data_ptr(), 1, self.cfg.vocab,
+                                    step["ids"].data_ptr()))
+        out = torch.empty(max_new, dtype=torch.int32, device=self.device)
+        out[0:1].copy_(step["ids"])
+        eos = set(self.cfg.eos_tokens)
+        produced = max_new
+        for i in range(1, max_new):
+            if eos and int(out[i - 1].item()) in eos:
+                produced = i
+                break
+            self.graph.replay()
+            self.length += 1
+            out[i:i + 1].copy_(step["ids"])
+        return [int(t) for t in out[:produced].tolist()]
+
+    def device_status(self) -> int:
+        bad = int(self.error_flag.item())
+        if bad:
+            raise LeafError(_lib.LEAFQ_ERR_INVALID, "token id exceeds vocabulary")
+        return self.lib.leafq_device_status()

@@ -57,6 +57,7 @@ def lib() -> ctypes.CDLL:
                                          ctypes.c_uint, _c_size, _vp, _vp, _vp, ctypes.c_int]
         _lib.oq_linear_int.argtypes = [_vp, _c_size, _c_size, _vp, _vp, _c_size, ctypes.c_uint,
                                        _c_size, _vp, _vp, _vp, ctypes.c_int]
+        _lib.oq_expf.argtypes = [_vp, _vp, _c_size]
         _lib.oq_linear_float.argtypes = [_vp, _c_size, _c_size, _vp, _vp, _c_size, ctypes.c_uint,
                                          _c_size, _vp, _vp]
         _lib.oq_graph_quantize.argtypes = [_vp, _c_size, ctypes.c_float, _vp]
@@ -200,6 +201,14 @@ def linear_float(x, weight, scales, bits, group, bias=None):
                                    _p(bias), _p(y))
     if status:
         raise ValueError(f"oq_linear_float failed ({status})")
+    return y
+
+
+def expf(x):
+    """libm expf elementwise (float32 in, float32 out)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty_like(x)
+    lib().oq_expf(_p(x), _p(y), x.size)
     return y
 
 

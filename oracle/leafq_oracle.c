@@ -202,3 +202,9 @@ void oq_gemm_i8_per_channel(const int8_t* a, const int8_t* b, const float* bias,
             out[row * n + col] = value;
         }
 }
+
+/* libm expf over an array: the exponential the reference's attention
+ * (transformer.cpp:130) and scalar SiLU (decoder.cpp:983) call on Linux. */
+void oq_expf(const float* x, float* y, size_t n) {
+    for (size_t i = 0; i < n; ++i) y[i] = expf(x[i]);
+}

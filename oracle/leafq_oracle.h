@@ -57,6 +57,10 @@ void oq_gemm_i8_per_channel(const int8_t* a, const int8_t* b, const float* bias,
                             const float* weight_scales, float* out, size_t m, size_t k, size_t n,
                             int relu);
 
+/* y[i] = expf(x[i]) (libm): the reference decoder's attention and SiLU
+ * exponential on Linux (transformer.cpp:130, decoder.cpp:983). */
+void oq_expf(const float* x, float* y, size_t n);
+
 #ifdef __cplusplus
 }
 #endif

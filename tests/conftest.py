@@ -6,8 +6,9 @@ import pytest
 
 REPO = Path(__file__).resolve().parents[1]
 GOLDEN = REPO / "tests" / "golden"
-if str(REPO) not in sys.path:
-    sys.path.insert(0, str(REPO))
+for _path in (REPO, GOLDEN):
+    if str(_path) not in sys.path:
+        sys.path.insert(0, str(_path))
 
 
 def pytest_configure(config):

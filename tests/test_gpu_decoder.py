@@ -1,0 +1,98 @@
+"""The GPU decoder against the reference decoder (oracle/_ref/leaf_decoder
+outputs recorded by tests/golden/make_decoder_golden.py): identical greedy
+tokens and bit-identical logits (prefill and every decode step).
+"""
+import hashlib
+import json
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN
+import decoder_fixture as fx  # tests/golden
+
+pytestmark = pytest.mark.gpu
+
+def _artifact(tmp_path, name, shape):
+    meta = json.loads((GOLDEN / f"decoder_{name}.json").read_text())
+    path = tmp_path / f"{name}.leaf"
+    fx.write_artifact(path, shape, fx.llama_tensors(shape, meta["weight_seed"], meta["norm_noise"]),
+                      meta["bits"], meta["group"])
+    h = hashlib.sha256()
+    with path.open("rb") as f:
+        for block in iter(lambda: f.read(1 << 24), b""):
+            h.update(block)
+    assert h.hexdigest() == meta["artifact_sha256"], "fixture artifact differs from the reference export"
+    with np.load(GOLDEN / f"decoder_{name}.npz") as data:
+        golden = {k: data[k] for k in data.files}
+    return path, golden
+
+
+def _close(got, ref):
+    got = np.ascontiguousarray(got, dtype=np.float32)
+    ref = np.ascontiguousarray(ref, dtype=np.float32)
+    return np.array_equal(got.view(np.uint32), ref.view(np.uint32)), float(np.max(np.abs(got - ref)))
+
+
+@pytest.mark.parametrize("name", ["tiny_w8", "tiny_w4"])
+def test_tiny_decoder_matches_reference(cuda_device, tmp_path, name):
+    from leaf_b200.decoder import Decoder
+
+    path, golden = _artifact(tmp_path, name, fx.TINY)
+    dec = Decoder(path)
+    prompt, generated = golden["prompt"].tolist(), golden["generated"].tolist()
+    assert dec.generate(prompt, len(generated)) == generated
+    # Prefill logits of the prompt's last position (reference verify mode).
+    dec.reset()
+    ok, err = _close(dec.forward(prompt).cpu().numpy()[0], golden["prefill_logits"][-1])
+    assert ok, f"prefill logits differ by {err}"
+    # Token-by-token decode logits over prompt + generated (chunked mode).
+    dec.reset()
+    sequence = prompt + generated[:-1]
+    for i, tok in enumerate(sequence):
+        ok, err = _close(dec.forward([tok]).cpu().numpy()[0], golden["decode_logits"][i])
+        assert ok, f"decode logits at step {i} differ by {err}"
+    assert dec.device_status() == 0
+
+
+def test_tinyllama_greedy_tokens(cuda_device, tmp_path):
+    """Config 3: TinyLlama-1.1B-shape W8A8 decoder, 128-token random prompt,
+    128 greedy tokens, identical to the reference's."""
+    from leaf_b200.decoder import Decoder
+
+    path, golden = _artifact(tmp_path, "tinyllama_w8", fx.TINYLLAMA)
+    dec = Decoder(path)
+    path.unlink()
+    prompt, generated = golden["prompt"].tolist(), golden["generated"].tolist()
+    logits = dec.forward(prompt).cpu().numpy()[0]
+    ok, err = _close(logits, golden["prefill_last_logits"])
+    assert ok, f"prefill logits differ by {err}"
+    dec.reset()
+    got = dec.generate(prompt, len(generated))
+    assert got == generated, next(i for i, (a, b) in enumerate(zip(got, generated)) if a != b)
+    assert dec.device_status() == 0
+
+
+def test_expf_matches_libm(cuda_device):
+    """leafq_expf against the host libm expf: 32M random bit patterns plus
+    every float of [-2, -1) and [1, 2) and the whole softmax range near 0."""
+    import leaf_b200 as lq
+    import oracle
+
+    rng = np.random.default_rng(4)
+    parts = [rng.integers(0, 2**32, size=1 << 25, dtype=np.uint64).astype(np.uint32),
+             np.arange(0x3F800000, 0x40000000, dtype=np.uint32),
+             np.arange(0xBF800000, 0xC0000000, dtype=np.uint32),
+             np.arange(0xB8000000, 0xB8800000, dtype=np.uint32)]
+    bits = np.concatenate(parts)
+    x = bits.view(np.float32)
+    x = x[~np.isnan(x)]
+    expect = oracle.expf(x)
+    xd = torch.from_numpy(x).cuda()
+    y = torch.empty_like(xd)
+    lq._lib.check(lq.load().leafq_expf(torch.cuda.current_stream().cuda_stream, xd.data_ptr(), x.size,
+                                       y.data_ptr()))
+    got = y.cpu().numpy()
+    bad = np.flatnonzero(got.view(np.uint32) != expect.view(np.uint32))
+    assert bad.size == 0, (x[bad[:5]], got[bad[:5]], expect[bad[:5]])
