@@ -218,6 +218,63 @@ int leafq_linear_allgather(void* stream, leafq_allgather_t* ag, const float* x, 
 int leafq_allgather_destroy(leafq_allgather_t* ag);
 
 /* ------------------------------------------------------------------------
+ * Whole-model decode step.  One cooperative launch runs one token through
+ * every layer of a Llama-family W8A8 decoder (per-row INT8 linears and
+ * embedding; RMSNorm, RoPE, GQA attention over an fp32 KV cache, SiLU gate,
+ * sequential residual, final norm, lm_head) and the greedy argmax:
+ * Decoder::Impl::forward_into for one token (decoder.cpp:1282-1452) plus
+ * main_decoder.cpp:101.  Bit-identical to the reference.  The launch reads
+ * the token at *ids and the cache length at *position, appends to the
+ * caches, writes the logits (if given), sets *ids to the argmax, writes it to
+ * history[*position + 1] (if given) and increments *position -- so repeated
+ * launches (or replays of one captured launch) generate greedily with no
+ * host work.  Prefill (several tokens) uses the per-operator entry points,
+ * which share the caches and position. */
+typedef struct leafq_model_layer {
+    const float* input_norm;     /* fp32 [hidden] */
+    const float* post_norm;      /* fp32 [hidden] */
+    const int8_t* qkv;           /* [(heads + 2 kv_heads) * head_dim][hidden]: q, k, v rows stacked */
+    const float* qkv_scales;
+    const int8_t* o;             /* [hidden][hidden] */
+    const float* o_scales;
+    const int8_t* gate_up;       /* [2 * intermediate][hidden]: gate / up rows interleaved */
+    const float* gate_up_scales;
+    const int8_t* down;          /* [hidden][intermediate] */
+    const float* down_scales;
+    float* k_cache;              /* fp32 [kv_heads][capacity][head_dim] */
+    float* v_cache;
+} leafq_model_layer;
+
+typedef struct leafq_model_desc {
+    int32_t layers, hidden, intermediate, heads, kv_heads, head_dim, vocab;
+    int64_t capacity;            /* cache rows (<= 4096) */
+    float epsilon;               /* RMSNorm epsilon */
+    float embedding_scale;
+    float attn_scale;            /* 1 / sqrt(sqrt(head_dim)), applied to q.k twice */
+    const int8_t* embed;         /* [vocab][hidden], per-row scales */
+    const float* embed_scales;
+    const float* final_norm;
+    const int8_t* lm_head;       /* [vocab][hidden], per-row scales */
+    const float* lm_head_scales;
+    const float* cos_table;      /* [capacity][head_dim / 2] from leafq_rope_tables */
+    const float* sin_table;
+    const leafq_model_layer* layer;  /* host array [layers] */
+    int32_t* ids;                /* device [1] */
+    int32_t* position;           /* device [1] */
+    int32_t* history;            /* device [capacity] or NULL */
+    float* logits;               /* device [vocab] or NULL */
+} leafq_model_desc;
+
+typedef struct leafq_model_plan_t leafq_model_plan_t;
+
+/* Checks the geometry, allocates the plan's hand-off buffers on the current
+ * device and records the op list; pointers in desc must stay valid. */
+int leafq_model_plan_create(const leafq_model_desc* desc, leafq_model_plan_t** plan);
+/* One decode step (one cooperative launch of one block per SM). */
+int leafq_model_plan_run(void* stream, leafq_model_plan_t* plan);
+int leafq_model_plan_destroy(leafq_model_plan_t* plan);
+
+/* ------------------------------------------------------------------------
  * Decoder operators around the linears (Decoder::Impl::forward_into,
  * decoder.cpp:1282-1452), for a GPU port of the decode loop.  Device
  * pointers, fp32 activations, token-major rows.  `position` is a device
@@ -258,8 +315,9 @@ int leafq_rotary_append(void* stream, const float* qkv, int64_t tokens, int head
 int leafq_attention(void* stream, const float* q_heads, const float* k_cache, const float* v_cache,
                     int64_t tokens, int heads, int kv_heads, int dim, const int32_t* position,
                     int64_t capacity, float scale, float* out);
-/* gate_up [tokens][2 * width] (gate | up) -> out [tokens][width] =
- * up * (gate / (1 + expf(-gate))) (decoder.cpp:982-988, 1414). */
+/* gate_up [tokens][2 * width] with gate and up interleaved (g0, u0, g1, u1,
+ * ..., the output of one linear over interleaved gate / up rows) -> out
+ * [tokens][width] = u * (g / (1 + expf(-g))) (decoder.cpp:982-988, 1414). */
 int leafq_silu_gate(void* stream, const float* gate_up, int64_t tokens, int64_t width, float* out);
 /* ids[r] = first index of the largest value of logits row r
  * (std::max_element, main_decoder.cpp:101). */

@@ -56,6 +56,9 @@ _SIGNATURES = {
     "leafq_linear_allgather": ([_vp, _vp, _vp, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _int, _i64,
                                 _int, _vp, _vp, _vp, _size, _u32], _int),
     "leafq_allgather_destroy": ([_vp], _int),
+    "leafq_model_plan_create": ([_vp, _vp], _int),
+    "leafq_model_plan_run": ([_vp, _vp], _int),
+    "leafq_model_plan_destroy": ([_vp], _int),
     "leafq_embed": ([_vp, _vp, _i64, _vp, _vp, _int, _i64, _i64, _i64, _f32, _vp, _vp], _int),
     "leafq_rmsnorm": ([_vp, _vp, _vp, _int, _i64, _i64, _vp, _f32, _vp], _int),
     "leafq_rope_tables": ([_f32, _int, _i64, _vp, _vp], _int),
@@ -75,6 +78,29 @@ class DecodeOp(ctypes.Structure):
     _fields_ = [("x", _vp), ("y", _vp), ("weight", _vp), ("weight_scales", _vp), ("bias", _vp),
                 ("rows", _i64), ("cols", _i64), ("wait", ctypes.c_int32),
                 ("x_offset", ctypes.c_int32)]
+
+
+
+class ModelLayer(ctypes.Structure):
+    """leafq_model_layer (include/leafq.h)."""
+
+    _fields_ = [(name, _vp) for name in (
+        "input_norm", "post_norm", "qkv", "qkv_scales", "o", "o_scales", "gate_up",
+        "gate_up_scales", "down", "down_scales", "k_cache", "v_cache")]
+
+
+class ModelDesc(ctypes.Structure):
+    """leafq_model_desc (include/leafq.h)."""
+
+    _fields_ = [("layers", ctypes.c_int32), ("hidden", ctypes.c_int32),
+                ("intermediate", ctypes.c_int32), ("heads", ctypes.c_int32),
+                ("kv_heads", ctypes.c_int32), ("head_dim", ctypes.c_int32),
+                ("vocab", ctypes.c_int32), ("capacity", _i64), ("epsilon", _f32),
+                ("embedding_scale", _f32), ("attn_scale", _f32)] + [
+        (name, _vp) for name in ("embed", "embed_scales", "final_norm", "lm_head", "lm_head_scales",
+                                 "cos_table", "sin_table", "layer", "ids", "position", "history",
+                                 "logits")]
+
 
 _lib = None
 

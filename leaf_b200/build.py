@@ -19,7 +19,7 @@ CSRC = PACKAGE / "csrc"
 LIBRARY = PACKAGE / "libleafq.so"
 SOURCES = ["act_quant.cu", "gemv_w8a8.cu", "gemv_w4a32.cu", "linear_generic.cu", "gemm_tc.cu",
            "graph_gemm.cu", "api.cu", "static_scratch.cu", "decode_persistent.cu",
-           "peer_allgather.cu", "decoder_ops.cu"]
+           "peer_allgather.cu", "decoder_ops.cu", "decode_model.cu"]
 GENCODE = "arch=compute_100a,code=sm_100a"
 
 

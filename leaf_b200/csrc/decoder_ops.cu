@@ -38,51 +38,16 @@
 #include <cmath>
 #include <cstring>
 
+#include "decoder_math.cuh"
 #include "leafq_device.cuh"
 #include "leafq_internal.h"
 
 namespace leafq {
 namespace {
 
-struct ExpTable {
-    unsigned long long bits[32];
-};
-
 constexpr int kNormThreads = 256;
 constexpr int kAttnThreads = 128;
 constexpr int kArgmaxThreads = 1024;
-
-// expf of the system libm (see the file comment).  tab.bits[i] = bits of
-// 2^(i/32) rounded to double, minus i << 47.
-__device__ __forceinline__ float expf_libm(float x, const ExpTable& tab) {
-    const uint32_t ux = __float_as_uint(x);
-    const uint32_t abstop = (ux >> 20) & 0x7ffu;
-    if (abstop >= 0x42bu) {  // |x| >= 88 (top 12 bits of 88.0f), inf, nan
-        if (ux == 0xff800000u) return 0.0f;
-        if (abstop >= 0x7f8u) return __fadd_rn(x, x);
-        if (x > 0x1.62e42ep6f) return __int_as_float(0x7f800000);
-        if (x < -0x1.9fe368p6f) return 0.0f;
-    }
-    const double inv_ln2_n = 0x1.71547652b82fep+0 * 32.0;
-    const double shift = 0x1.8p+52;
-    const double xd = static_cast<double>(x);
-    double kd = __fma_rn(inv_ln2_n, xd, shift);
-    const unsigned long long ki = static_cast<unsigned long long>(__double_as_longlong(kd));
-    kd = __dsub_rn(kd, shift);
-    const double r = __fma_rn(inv_ln2_n, xd, -kd);
-    unsigned long long t = tab.bits[ki % 32];
-    t += ki << 47;
-    const double sc = __longlong_as_double(static_cast<long long>(t));
-    const double c0 = 0x1.c6af84b912394p-5 / 32.0 / 32.0 / 32.0;
-    const double c1 = 0x1.ebfce50fac4f3p-3 / 32.0 / 32.0;
-    const double c2 = 0x1.62e42ff0c52d6p-1 / 32.0;
-    const double z = __fma_rn(c0, r, c1);
-    const double r2 = __dmul_rn(r, r);
-    double y = __fma_rn(c2, r, 1.0);
-    y = __fma_rn(z, r2, y);
-    y = __dmul_rn(y, sc);
-    return __double2float_rn(y);
-}
 
 __device__ __forceinline__ float block_max(float v, float* scratch) {
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -139,6 +104,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(
     extern __shared__ float row[];  // [width] values, then [width] squares
     float* squares = row + width;
     __shared__ float total;
+    __shared__ SumScratch sum_scratch;
     const int64_t t = blockIdx.x;
     float* h = hidden + t * width;
     for (int64_t c = threadIdx.x; c < width; c += blockDim.x) {
@@ -153,18 +119,13 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(
         squares[c] = __fmul_rn(v, v);
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
+    if (width <= 8 * kNormThreads) {
+        const float sq = sum_squares_sequential_order<kNormThreads>(
+            row, static_cast<int>(width), &sum_scratch, static_cast<int>(threadIdx.x), [] { __syncthreads(); });
+        if (threadIdx.x == 0) total = sq;
+    } else if (threadIdx.x == 0) {
         float sq = 0.0f;
-        int64_t c = 0;
-        if ((width & 3) == 0)
-            for (; c + 4 <= width; c += 4) {
-                const float4 q = *reinterpret_cast<const float4*>(squares + c);
-                sq = __fadd_rn(sq, q.x);
-                sq = __fadd_rn(sq, q.y);
-                sq = __fadd_rn(sq, q.z);
-                sq = __fadd_rn(sq, q.w);
-            }
-        for (; c < width; ++c) sq = __fadd_rn(sq, squares[c]);
+        for (int64_t c = 0; c < width; ++c) sq = __fadd_rn(sq, squares[c]);
         total = sq;
     }
     __syncthreads();
@@ -270,15 +231,16 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
 }
 
 // -------------------------------------------------------------- silu gate
-// gate_up[t] = [gate (width) | up (width)]; out[t][j] = up * (g / (1 + expf(-g))).
+// gate_up[t] = [g0, u0, g1, u1, ...] (gate and up rows interleaved);
+// out[t][j] = u_j * (g_j / (1 + expf(-g_j))).
 __global__ void silu_gate_kernel(const float* __restrict__ gate_up, int64_t tokens, int64_t width,
                                  float* __restrict__ out, const __grid_constant__ ExpTable tab) {
     const int64_t n = tokens * width;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t t = i / width, j = i - t * width;
-        const float g = gate_up[t * 2 * width + j];
-        const float u = gate_up[t * 2 * width + width + j];
+        const float2 gu = reinterpret_cast<const float2*>(gate_up)[t * width + j];
+        const float g = gu.x, u = gu.y;
         out[i] = __fmul_rn(u, __fdiv_rn(g, __fadd_rn(1.0f, expf_libm(-g, tab))));
     }
 }
@@ -332,21 +294,6 @@ __global__ void expf_kernel(const float* __restrict__ x, int64_t n, float* __res
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x)
         y[i] = expf_libm(x[i], tab);
-}
-
-// 2^(i/32) rounded to double, minus i << 47 (the table of expf_libm).
-const ExpTable& exp_table() {
-    static const ExpTable table = [] {
-        ExpTable t;
-        for (int i = 0; i < 32; ++i) {
-            const double v = static_cast<double>(std::exp2(static_cast<long double>(i) / 32.0L));
-            unsigned long long bits;
-            std::memcpy(&bits, &v, sizeof(bits));
-            t.bits[i] = bits - (static_cast<unsigned long long>(i) << 47);
-        }
-        return t;
-    }();
-    return table;
 }
 
 }  // namespace

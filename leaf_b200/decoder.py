@@ -7,9 +7,10 @@ RoPE + KV append -> attention -> o -> residual + RMSNorm -> gate|up -> SiLU
 gate -> down -> residual (+ next RMSNorm), final RMSNorm, lm_head on the last
 row.  Every linear is ``leafq_linear`` (W8A8 / W4A8 with activation_bits 8,
 weight-only with 32); the other operators are the library's decoder kernels.
-q, k and v (and gate and up) run as one linear over their concatenated rows
--- rows are independent, so the outputs are bit-identical to the separate
-calls the reference makes.  ``generate`` is the greedy loop of
+q, k and v run as one linear over their stacked rows, gate and up as one
+linear over their interleaved rows (gate_0, up_0, gate_1, ...) -- rows are
+independent, so the outputs are bit-identical to the separate calls the
+reference makes.  ``generate`` is the greedy loop of
 main_decoder.cpp:95-113: one prefill forward, then one CUDA-graph replay per
 token with the argmax, the next embedding and the position update on the
 device (no host round trip per token).
@@ -36,12 +37,19 @@ def _stream() -> int:
     return torch.cuda.current_stream().cuda_stream
 
 
-def _concat_rows(parts: list[HostTensor]) -> tuple:
+def _concat_rows(parts: list[HostTensor], interleave: bool = False) -> tuple:
+    """Rows of several equally quantised matrices as one: stacked (q | k | v)
+    or, with interleave, alternating (gate_0, up_0, gate_1, up_1, ...)."""
     bits, group, cols = parts[0].bits, parts[0].group, parts[0].cols
     if any(p.bits != bits or p.group != group or p.cols != cols for p in parts):
         raise LeafError(_lib.LEAFQ_ERR_UNSUPPORTED, "fused projections need one precision and group")
-    data = np.concatenate([np.asarray(p.data) for p in parts], axis=0)
-    scales = None if bits == 32 else np.concatenate([np.asarray(p.scales) for p in parts], axis=0)
+    if interleave:
+        data = np.stack([np.asarray(p.data) for p in parts], axis=1).reshape(-1, parts[0].data.shape[1])
+        scales = (None if bits == 32 else
+                  np.stack([np.asarray(p.scales) for p in parts], axis=1).reshape(-1, parts[0].scales.shape[1]))
+    else:
+        data = np.concatenate([np.asarray(p.data) for p in parts], axis=0)
+        scales = None if bits == 32 else np.concatenate([np.asarray(p.scales) for p in parts], axis=0)
     return data, scales, sum(p.rows for p in parts), cols, bits, group
 
 
@@ -68,8 +76,8 @@ class Decoder:
         def f32(t: HostTensor):
             return torch.from_numpy(np.array(t.data, dtype=np.float32).reshape(-1)).to(dev)
 
-        def weight(parts):
-            data, scales, rows, cols, bits, group = _concat_rows(parts)
+        def weight(parts, interleave=False):
+            data, scales, rows, cols, bits, group = _concat_rows(parts, interleave)
             w = QuantWeight.from_host(data, scales, rows, cols, bits, group, device=dev)
             w.check()
             return w
@@ -89,7 +97,8 @@ class Decoder:
                 qkv=weight([get(p + "self_attn.q_proj.weight"), get(p + "self_attn.k_proj.weight"),
                             get(p + "self_attn.v_proj.weight")]),
                 o=weight([get(p + "self_attn.o_proj.weight")]),
-                gate_up=weight([get(p + "mlp.gate_proj.weight"), get(p + "mlp.up_proj.weight")]),
+                gate_up=weight([get(p + "mlp.gate_proj.weight"), get(p + "mlp.up_proj.weight")],
+                               interleave=True),
                 down=weight([get(p + "mlp.down_proj.weight")]),
             ))
             for name in ("q", "k", "v", "o"):
@@ -115,6 +124,11 @@ class Decoder:
         self.length = 0
         self._buffers: dict[int, dict] = {}
         self.graph: Optional[torch.cuda.CUDAGraph] = None
+        self.token = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.history = torch.zeros(self.capacity + 1, dtype=torch.int32, device=dev)
+        self.step_logits = torch.zeros(cfg.vocab, dtype=torch.float32, device=dev)
+        self._plan = None
+        self._plan_refs = None
 
     # ------------------------------------------------------------ buffers
     def _bufs(self, tokens: int) -> dict:
@@ -269,6 +283,72 @@ class Decoder:
             self.length += 1
             out[i:i + 1].copy_(step["ids"])
         return [int(t) for t in out[:produced].tolist()]
+
+    # ------------------------------------------------ whole-step kernel
+    def fused_supported(self) -> bool:
+        """The one-launch decode step needs per-row INT8 weights and
+        embedding, W8A8, and a cache of at most 4096 rows."""
+        per_row = all(w.bits == 8 and w.group == w.cols for w in self._weights())
+        return (per_row and self.activation_bits == 8 and self.embed_bits == 8 and
+                self.embed_group == self.cfg.hidden and self.capacity <= 4096 and
+                self.final_norm is not None)
+
+    def build_fused(self) -> None:
+        """Create the leafq_model_plan for this decoder (one cooperative
+        launch per generated token)."""
+        if not self.fused_supported():
+            raise LeafError(_lib.LEAFQ_ERR_UNSUPPORTED,
+                            "one-launch decode needs per-row INT8 weights, W8A8 and capacity <= 4096")
+        c, ptr = self.cfg, (lambda t: t.data_ptr())
+        layers = (_lib.ModelLayer * c.layers)()
+        for i, L in enumerate(self.layers):
+            layers[i] = _lib.ModelLayer(
+                ptr(L["input_norm"]), ptr(L["post_norm"]), ptr(L["qkv"].data), ptr(L["qkv"].scales),
+                ptr(L["o"].data), ptr(L["o"].scales), ptr(L["gate_up"].data), ptr(L["gate_up"].scales),
+                ptr(L["down"].data), ptr(L["down"].scales), ptr(self.k_cache[i]), ptr(self.v_cache[i]))
+        desc = _lib.ModelDesc(
+            c.layers, c.hidden, c.intermediate, c.heads, c.kv_heads, c.head_dim, c.vocab, self.capacity,
+            c.epsilon, c.embedding_scale, self.scale, ptr(self.embed_table), ptr(self.embed_scales),
+            ptr(self.final_norm), ptr(self.lm_head.data), ptr(self.lm_head.scales), ptr(self.cos),
+            ptr(self.sin), ctypes.cast(layers, ctypes.c_void_p), ptr(self.token), ptr(self.position),
+            ptr(self.history), ptr(self.step_logits))
+        plan = ctypes.c_void_p()
+        check(self.lib.leafq_model_plan_create(ctypes.byref(desc), ctypes.byref(plan)))
+        self._plan = plan
+        self._plan_refs = (layers, desc)
+
+    def step_fused(self) -> None:
+        """One decode step of the token in self.token at the device position
+        (one launch); the argmax replaces self.token."""
+        check(self.lib.leafq_model_plan_run(_stream(), self._plan))
+
+    def generate_fused(self, prompt, max_new: int) -> list[int]:
+        """Greedy continuation as generate(), with every decode step one
+        launch of the whole-model kernel."""
+        if self._plan is None:
+            self.build_fused()
+        n = self.length + len(prompt)
+        if n + max_new - 1 > min(self.cfg.max_positions, self.capacity):
+            raise LeafError(_lib.LEAFQ_ERR_INVALID, "context length exceeds artifact limit")
+        logits = self.forward(prompt)
+        check(self.lib.leafq_argmax(_stream(), logits.data_ptr(), 1, self.cfg.vocab,
+                                    self.token.data_ptr()))
+        self.history[n:n + 1].copy_(self.token)
+        for _ in range(max_new - 1):
+            self.step_fused()
+        self.length += max_new - 1
+        out = [int(t) for t in self.history[n:n + max_new].tolist()]
+        eos = set(self.cfg.eos_tokens)
+        for i, t in enumerate(out):
+            if t in eos:
+                return out[:i + 1]
+        return out
+
+    def close(self) -> None:
+        if self._plan is not None:
+            torch.cuda.synchronize(self.device)
+            check(self.lib.leafq_model_plan_destroy(self._plan))
+            self._plan = None
 
     def device_status(self) -> int:
         bad = int(self.error_flag.item())

@@ -56,6 +56,28 @@ def test_tiny_decoder_matches_reference(cuda_device, tmp_path, name):
     assert dec.device_status() == 0
 
 
+def test_tiny_fused_decode_step(cuda_device, tmp_path):
+    """The one-launch decode step: same tokens and bit-identical logits at
+    every step (W8A8 fixture)."""
+    from leaf_b200.decoder import Decoder
+
+    path, golden = _artifact(tmp_path, "tiny_w8", fx.TINY)
+    dec = Decoder(path)
+    prompt, generated = golden["prompt"].tolist(), golden["generated"].tolist()
+    assert dec.generate_fused(prompt, len(generated)) == generated
+    dec.reset()
+    n = len(prompt)
+    dec.forward(prompt)
+    for j, tok in enumerate(generated[:-1]):
+        dec.token.fill_(tok)
+        dec.step_fused()
+        ok, err = _close(dec.step_logits.cpu().numpy(), golden["decode_logits"][n + j])
+        assert ok, f"fused step {j} logits differ by {err}"
+        assert int(dec.token.item()) == generated[j + 1]
+    assert dec.device_status() == 0
+    dec.close()
+
+
 def test_tinyllama_greedy_tokens(cuda_device, tmp_path):
     """Config 3: TinyLlama-1.1B-shape W8A8 decoder, 128-token random prompt,
     128 greedy tokens, identical to the reference's."""
@@ -71,7 +93,11 @@ def test_tinyllama_greedy_tokens(cuda_device, tmp_path):
     dec.reset()
     got = dec.generate(prompt, len(generated))
     assert got == generated, next(i for i, (a, b) in enumerate(zip(got, generated)) if a != b)
+    dec.reset()
+    got = dec.generate_fused(prompt, len(generated))
+    assert got == generated, next(i for i, (a, b) in enumerate(zip(got, generated)) if a != b)
     assert dec.device_status() == 0
+    dec.close()
 
 
 def test_expf_matches_libm(cuda_device):

@@ -1,0 +1,113 @@
+"""Decoder operators through the C ABI against the CPU restatement
+(oracle/decoder.py, itself bit-exact against the reference decoder):
+RMSNorm (block-parallel sum in the reference's sequential rounding), RoPE +
+KV append, attention and the SiLU gate, bit for bit."""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+import leaf_b200 as lq
+import oracle
+from oracle import decoder as od
+
+pytestmark = pytest.mark.gpu
+
+
+def _s():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _vectors(rng, kind, rows, width):
+    g = rng.standard_normal((rows, width)).astype(np.float32)
+    if kind == "normal":
+        return g
+    if kind == "outliers":
+        g[rng.random(g.shape) < 0.01] *= 100
+        return g
+    if kind == "grid":  # exact low-precision values: many rounding ties
+        return (np.floor(g * 4) / 4).astype(np.float32)
+    if kind == "zeros":
+        g[rng.random(g.shape) < 0.3] = 0
+        return g
+    if kind == "tiny":  # squares in the subnormal range
+        return (g * np.float32(1e-20)).astype(np.float32)
+    if kind == "huge":  # sums overflow to inf
+        return (g * np.float32(1e18)).astype(np.float32)
+    if kind == "pow2":
+        return np.ldexp(np.float32(1), rng.integers(-10, 10, size=g.shape)).astype(np.float32)
+    raise ValueError(kind)
+
+
+@pytest.mark.parametrize("width", [64, 100, 2048, 3000])
+@pytest.mark.parametrize("kind", ["normal", "outliers", "grid", "zeros", "tiny", "huge", "pow2"])
+def test_rmsnorm_bit_exact(cuda_device, kind, width):
+    rng = np.random.default_rng(hash((kind, width)) % 2**32)
+    rows = 48
+    x = _vectors(rng, kind, rows, width)
+    delta = rng.standard_normal((rows, width)).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(width)).astype(np.float32)
+    for add_zero in (0, 1):
+        h = torch.from_numpy(x).cuda()
+        d = torch.from_numpy(delta).cuda()
+        out = torch.empty_like(h)
+        lq._lib.check(lq.load().leafq_rmsnorm(_s(), h.data_ptr(), d.data_ptr(), add_zero, rows, width,
+                                              torch.from_numpy(w).cuda().data_ptr(), ctypes.c_float(1e-5),
+                                              out.data_ptr()))
+        hx = x + ((delta + np.float32(0)) if add_zero else delta)
+        assert np.array_equal(h.cpu().numpy().view(np.uint32), hx.view(np.uint32))
+        with np.errstate(over="ignore", invalid="ignore"):
+            expect = od.rmsnorm(hx, w, 1e-5)
+        got = out.cpu().numpy()
+        assert np.array_equal(got.view(np.uint32), expect.view(np.uint32)), kind
+
+
+def test_rotary_attention_silu_bit_exact(cuda_device):
+    rng = np.random.default_rng(7)
+    heads, kv, dim, cap, tokens, start = 8, 2, 64, 256, 5, 37
+    c = od.rope_tables(10000.0, dim, cap)
+    cos, sin = (torch.from_numpy(t).cuda() for t in c)
+    qkv = rng.standard_normal((tokens, (heads + 2 * kv) * dim)).astype(np.float32)
+    kc = rng.standard_normal((kv, cap, dim)).astype(np.float32)
+    vc = rng.standard_normal((kv, cap, dim)).astype(np.float32)
+    pos = torch.tensor([start], dtype=torch.int32, device="cuda")
+    q_heads = torch.empty((heads, tokens, dim), device="cuda")
+    kd, vd = torch.from_numpy(kc).cuda(), torch.from_numpy(vc).cuda()
+    lib = lq.load()
+    lq._lib.check(lib.leafq_rotary_append(_s(), torch.from_numpy(qkv).cuda().data_ptr(), tokens, heads, kv,
+                                          dim, dim, cos.data_ptr(), sin.data_ptr(), pos.data_ptr(),
+                                          q_heads.data_ptr(), kd.data_ptr(), vd.data_ptr(), cap))
+    # oracle: the same rotation and append
+    dec = od.OracleDecoder.__new__(od.OracleDecoder)
+    dec.c = type("C", (), {"head_dim": dim, "rotary_dim": dim})()
+    dec.cos, dec.sin = c
+    qh = dec._rotate(qkv[:, :heads * dim], tokens, heads, start)
+    kh = dec._rotate(qkv[:, heads * dim:(heads + kv) * dim], tokens, kv, start)
+    vh = qkv[:, (heads + kv) * dim:].reshape(tokens, kv, dim).transpose(1, 0, 2)
+    kc[:, start:start + tokens] = kh
+    vc[:, start:start + tokens] = vh
+    assert np.array_equal(q_heads.cpu().numpy().view(np.uint32), qh.view(np.uint32))
+    assert np.array_equal(kd.cpu().numpy().view(np.uint32), kc.view(np.uint32))
+    assert np.array_equal(vd.cpu().numpy().view(np.uint32), vc.view(np.uint32))
+    scale = float(np.float32(1) / np.sqrt(np.sqrt(np.float32(dim))))
+    out = torch.empty((tokens, heads * dim), device="cuda")
+    lq._lib.check(lib.leafq_attention(_s(), q_heads.data_ptr(), kd.data_ptr(), vd.data_ptr(), tokens, heads,
+                                      kv, dim, pos.data_ptr(), cap, ctypes.c_float(scale), out.data_ptr()))
+    sc = np.float32(scale)
+    expect = np.zeros((tokens, heads * dim), np.float32)
+    for h in range(heads):
+        for t in range(tokens):
+            n = start + t + 1
+            s = (od.attention_dot(qh[h, t], kc[h // (heads // kv), :n]) * sc) * sc
+            e = oracle.expf(s - s.max())
+            expect[t, h * dim:(h + 1) * dim] = od.seq_sum((e / od.seq_sum(e))[:, None] * vc[h // (heads // kv), :n],
+                                                          axis=0)
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), expect.view(np.uint32))
+    # SiLU gate over interleaved gate / up rows.
+    gu = (rng.standard_normal((3, 2 * 1000)) * 4).astype(np.float32)
+    act = torch.empty((3, 1000), device="cuda")
+    lq._lib.check(lib.leafq_silu_gate(_s(), torch.from_numpy(gu).cuda().data_ptr(), 3, 1000, act.data_ptr()))
+    g, u = gu[:, 0::2], gu[:, 1::2]
+    expect = u * (g / (np.float32(1) + oracle.expf(-g)))
+    assert np.array_equal(act.cpu().numpy().view(np.uint32), expect.view(np.uint32))
