@@ -49,13 +49,16 @@ constexpr int kRowsPerStage = 8;  // = warps per consumer group
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kNC = kConsumerWarps * 32;  // consumer threads
 constexpr uint32_t kRingBytes = 192 * 1024;
+// Blocks that run attention give the last 64 KB of their ring to it: with the
+// codes buffer and the scratch behind it, 88 KB of keys / values / scores.
+constexpr uint32_t kAttnRingBytes = 128 * 1024;
 constexpr int kStageBarriers = 16;
 constexpr int kMaxCols = 8192;
 constexpr int kXVec = kMaxCols / 4 / kNC;
 constexpr int kScratchFloats = 4096;  // hidden row for RMSNorm; attention scores + V chunk
 constexpr int kMaxCapacity = 2048;    // attention scores (first half of the scratch)
-constexpr int kChunkFloats = kScratchFloats - kMaxCapacity;  // staged V rows
 constexpr int kMaxDim = 256;
+constexpr int kAttFloats = static_cast<int>((kRingBytes - kAttnRingBytes) / 4) + kMaxCols / 4 + kScratchFloats;
 constexpr int kMaxOps = 1024;
 
 enum : int32_t { kOpLinear = 0, kOpAttention = 1 };
@@ -92,8 +95,8 @@ struct Model {
 };
 
 constexpr size_t kSmemBytes = (size_t)kRingBytes + kMaxCols + kScratchFloats * 4 + 3 * kMaxDim * 4 +
-                              2 * kStageBarriers * 8 + kStageBarriers * 8 + 2 * 2 * 8 * 4 +
-                              kConsumerWarps * 12 + 64 + sizeof(SumScratch) + 16;
+                              2 * (kStageBarriers + 2) * 8 + kStageBarriers * 8 + 2 * 2 * 8 * 4 +
+                              kConsumerWarps * 12 + 64;
 
 __device__ __forceinline__ void consumer_sync() {
     asm volatile("bar.sync 1, %0;" ::"n"(kNC) : "memory");
@@ -224,9 +227,10 @@ __device__ __forceinline__ float load_row_scale(const MOp& op, const OpGeometry&
 struct RingCursor {
     uint64_t head = 0;
     uint32_t off = 0;
+    uint32_t size = kRingBytes;
     __device__ __forceinline__ uint32_t place(uint32_t bytes) {
-        if (off + bytes > kRingBytes) {
-            head += kRingBytes - off;
+        if (off + bytes > size) {
+            head += size - off;
             off = 0;
         }
         const uint32_t start = off;
@@ -257,7 +261,8 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
     float* scratch = reinterpret_cast<float*>(codes + kMaxCols);      // [kScratchFloats]
     float* qkv_s = scratch + kScratchFloats;                           // q, k, v [3][kMaxDim]
     uint64_t* full = reinterpret_cast<uint64_t*>(qkv_s + 3 * kMaxDim);
-    uint64_t* empty = full + kStageBarriers;
+    uint64_t* att_bar = full + kStageBarriers;  // [2] attention K / V staging
+    uint64_t* empty = att_bar + 2;
     uint64_t* stage_end = empty + kStageBarriers;
     float* pair_y = reinterpret_cast<float*>(stage_end + kStageBarriers);  // [2 buf][2 group][8]
     float* partial_max = pair_y + 32;                                   // [kConsumerWarps]
@@ -265,7 +270,6 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
     int32_t* best_row = reinterpret_cast<int32_t*>(best_v + kConsumerWarps);
     float* total_s = reinterpret_cast<float*>(best_row + kConsumerWarps);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(total_s + 1);
-    SumScratch* sum_scratch = reinterpret_cast<SumScratch*>(smem + kSmemBytes - sizeof(SumScratch) - 16);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tid = threadIdx.x;
@@ -274,6 +278,8 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
             mbar_init(&full[b], 1);
             mbar_init(&empty[b], kRowsPerStage);
         }
+        mbar_init(&att_bar[0], 1);
+        mbar_init(&att_bar[1], 1);
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -293,6 +299,7 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
         if (lane == 0) {
             const uint64_t policy = l2_policy_evict_first();
             RingCursor cursor;
+            cursor.size = my_head(m.heads) >= 0 ? kAttnRingBytes : kRingBytes;
             uint64_t released = 0;
             int s = 0, rel = 0;
             bool go = true;
@@ -303,7 +310,7 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
                 for (int rb = 0; rb < g.nblocks; ++rb, ++s) {
                     const uint32_t bytes = static_cast<uint32_t>(block_rows(g, rb) * op.cols);
                     const uint32_t start = cursor.place(bytes);
-                    while (cursor.head - released > kRingBytes || s - rel >= kStageBarriers) {
+                    while (cursor.head - released > cursor.size || s - rel >= kStageBarriers) {
                         const int b = rel % kStageBarriers;
                         if (!mbar_wait(&empty[b], (rel / kStageBarriers) & 1, kSiteDecodeEmpty)) {
                             go = false;
@@ -330,19 +337,48 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
     const int head = my_head(m.heads);
     int s = 0;
     RingCursor cursor;
+    cursor.size = head >= 0 ? kAttnRingBytes : kRingBytes;
     bool ok = true;
     int prefetched_j = -1;
     float next_scale = 0.0f;
+    uint32_t att_uses[2] = {0u, 0u};  // completed phases of att_bar[0 / 1]
     for (int j = 0; j < nops; ++j) {
         const MOp op = ops[j];
         if (op.kind == kOpAttention) {
             if (head < 0) continue;
             // ---------------------------------------------- attention
+            // Cached keys / values of rows [0, pos) are staged through the
+            // attention region (the ring's last 64 KB, the codes buffer and
+            // the scratch: free in this block now) in chunks of C rows, one
+            // bulk copy per chunk; chunk 0 of both is requested before the
+            // wait for this token's q, k, v.
             const int dim = m.dim, half = dim / 2;
             const int kvh = head / (m.heads / m.kv_heads);
             float* qs = qkv_s;
             float* ks = qkv_s + kMaxDim;
             float* vs = qkv_s + 2 * kMaxDim;
+            float* kc = op.k_cache + (int64_t)kvh * m.capacity * dim;
+            float* vc = op.v_cache + (int64_t)kvh * m.capacity * dim;
+            const int64_t keys = pos + 1;
+            float* att = reinterpret_cast<float*>(ring + kAttnRingBytes);
+            const int keys_r = static_cast<int>((keys + 3) & ~3);
+            float* scores = att;
+            const int chunk = static_cast<int>(min64((kAttFloats - keys_r) / (2 * dim), pos > 0 ? pos : 1));
+            float* kbuf = att + keys_r;
+            float* vbuf = kbuf + chunk * dim;
+            const uint64_t keep = l2_policy_evict_last();
+            const int nchunks = static_cast<int>((pos + chunk - 1) / chunk);
+            auto issue = [&](const float* base, float* dst, uint64_t* bar, int c) {
+                const int64_t k0 = (int64_t)c * chunk;
+                const uint32_t bytes = static_cast<uint32_t>(min64(chunk, pos - k0) * dim * sizeof(float));
+                mbar_arrive_expect_tx(bar, bytes);
+                bulk_copy_g2s(dst, base + k0 * dim, bytes, bar, keep);
+            };
+            consumer_sync();  // every warp is done with the previous linear's codes
+            if (tid == 0 && nchunks > 0) {
+                issue(kc, kbuf, &att_bar[0], 0);
+                issue(vc, vbuf, &att_bar[1], 0);
+            }
             for (int i = tid; i < 3 * dim; i += kNC) {
                 const int part = i / dim, d = i % dim;
                 const int64_t src = part == 0 ? (int64_t)head * dim + d
@@ -356,7 +392,6 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
                 qkv_s[part * kMaxDim + d] = v;
             }
             consumer_sync();
-            if (*abort_flag) return;
             // RoPE on q and k (decoder.cpp:1271-1279), in place.
             if (tid < half) {
                 const float c = m.cos_table[pos * half + tid], sn = m.sin_table[pos * half + tid];
@@ -368,44 +403,44 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
                 ks[tid + half] = __fadd_rn(__fmul_rn(kb, c), __fmul_rn(ka, sn));
             }
             consumer_sync();
-            float* kc = op.k_cache + (int64_t)kvh * m.capacity * dim;
-            float* vc = op.v_cache + (int64_t)kvh * m.capacity * dim;
             if (head % (m.heads / m.kv_heads) == 0)
                 for (int d = tid; d < dim; d += kNC) {
                     kc[pos * dim + d] = ks[d];
                     vc[pos * dim + d] = vs[d];
                 }
-            // scores[k] = (q.k * scale) * scale, q.k summed left to right.
-            // A thread takes whole keys: the key row is loaded in one batch
-            // of float4s, then summed.
-            float* scores = scratch;
-            const int64_t keys = pos + 1;
+            // scores[k] = (q.k * scale) * scale with q.k summed left to right.
             float local_max = -INFINITY;
-            for (int64_t k = tid; k < keys; k += kNC) {
-                float dot = 0.0f;
-                if (k == pos) {
-                    for (int d = 0; d < dim; ++d) dot = __fadd_rn(dot, __fmul_rn(qs[d], ks[d]));
-                } else {
-                    const float4* krow = reinterpret_cast<const float4*>(kc + k * dim);
-                    for (int d0 = 0; d0 < dim; d0 += 32) {
-                        float4 kv[8];
-#pragma unroll
-                        for (int t = 0; t < 8; ++t)
-                            kv[t] = d0 + 4 * t < dim ? __ldcg(krow + d0 / 4 + t) : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-                        for (int t = 0; t < 8; ++t) {
-                            const int d = d0 + 4 * t;
-                            if (d < dim) {
-                                dot = __fadd_rn(dot, __fmul_rn(qs[d], kv[t].x));
-                                dot = __fadd_rn(dot, __fmul_rn(qs[d + 1], kv[t].y));
-                                dot = __fadd_rn(dot, __fmul_rn(qs[d + 2], kv[t].z));
-                                dot = __fadd_rn(dot, __fmul_rn(qs[d + 3], kv[t].w));
-                            }
-                        }
-                    }
+            for (int c = 0; c < nchunks; ++c) {
+                const int64_t k0 = (int64_t)c * chunk;
+                const int nk = static_cast<int>(min64(chunk, pos - k0));
+                if (c > 0 && tid == 0) issue(kc, kbuf, &att_bar[0], c);
+                if (ok && !mbar_wait(&att_bar[0], att_uses[0] & 1, kSiteDecodeFull)) {
+                    ok = false;
+                    *abort_flag = 1;
                 }
+                ++att_uses[0];
+                for (int k = tid; k < nk; k += kNC) {
+                    if (!ok) break;
+                    const float* krow = kbuf + k * dim;
+                    float dot = 0.0f;
+                    for (int d = 0; d < dim; d += 4) {
+                        const float4 kv = *reinterpret_cast<const float4*>(krow + d);
+                        dot = __fadd_rn(dot, __fmul_rn(qs[d], kv.x));
+                        dot = __fadd_rn(dot, __fmul_rn(qs[d + 1], kv.y));
+                        dot = __fadd_rn(dot, __fmul_rn(qs[d + 2], kv.z));
+                        dot = __fadd_rn(dot, __fmul_rn(qs[d + 3], kv.w));
+                    }
+                    const float sc = __fmul_rn(__fmul_rn(dot, m.attn_scale), m.attn_scale);
+                    scores[k0 + k] = sc;
+                    local_max = fmaxf(local_max, sc);
+                }
+                consumer_sync();  // chunk consumed
+            }
+            if (tid == kNC - 1) {  // the current token's key, from shared memory
+                float dot = 0.0f;
+                for (int d = 0; d < dim; ++d) dot = __fadd_rn(dot, __fmul_rn(qs[d], ks[d]));
                 const float sc = __fmul_rn(__fmul_rn(dot, m.attn_scale), m.attn_scale);
-                scores[k] = sc;
+                scores[pos] = sc;
                 local_max = fmaxf(local_max, sc);
             }
 #pragma unroll
@@ -433,22 +468,23 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
             consumer_sync();
             const float den = *total_s;
             for (int64_t k = tid; k < keys; k += kNC) scores[k] = __fdiv_rn(scores[k], den);
-            // out[d] = sum over keys, in order, of probability * v[k][d]: V is
-            // staged in shared memory a chunk of keys at a time by all
-            // threads; thread d then adds the chunk's terms in order.
-            float* vchunk = scratch + kMaxCapacity;
-            const int chunk_keys = kChunkFloats / dim;
+            consumer_sync();
+            // out[d] = sum over keys, in order, of probability * v[k][d].
             float acc = 0.0f;
-            for (int64_t k0 = 0; k0 < pos; k0 += chunk_keys) {
-                const int nk = static_cast<int>(min64(chunk_keys, pos - k0));
-                consumer_sync();  // previous chunk consumed (and scores final)
-                const float4* src = reinterpret_cast<const float4*>(vc + k0 * dim);
-                for (int i = tid; i < nk * dim / 4; i += kNC)
-                    reinterpret_cast<float4*>(vchunk)[i] = __ldcg(src + i);
-                consumer_sync();
-                if (tid < dim)
-                    for (int k = 0; k < nk; ++k)
-                        acc = __fadd_rn(acc, __fmul_rn(scores[k0 + k], vchunk[k * dim + tid]));
+            for (int c = 0; c < nchunks; ++c) {
+                const int64_t k0 = (int64_t)c * chunk;
+                const int nk = static_cast<int>(min64(chunk, pos - k0));
+                if (c > 0 && tid == 0) issue(vc, vbuf, &att_bar[1], c);
+                if (ok && !mbar_wait(&att_bar[1], att_uses[1] & 1, kSiteDecodeFull)) {
+                    ok = false;
+                    *abort_flag = 1;
+                }
+                ++att_uses[1];
+                if (ok && tid < dim) {
+                    const float* vb = vbuf + tid;
+                    for (int k = 0; k < nk; ++k) acc = __fadd_rn(acc, __fmul_rn(scores[k0 + k], vb[k * dim]));
+                }
+                consumer_sync();  // chunk consumed
             }
             if (tid < dim) {
                 acc = __fadd_rn(acc, __fmul_rn(scores[pos], vs[tid]));
@@ -458,6 +494,22 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
             continue;
         }
         // ---------------------------------------------------- linear
+        // The next attention's cached keys and values (written by earlier
+        // launches, likely evicted by the weight stream) are pulled into L2
+        // while this linear runs.
+        if (head >= 0 && tid == 0 && j + 1 < nops && pos > 0) {
+            const MOp nx = ops[j + 1];
+            if (nx.kind == kOpAttention) {
+                const int kvh = head / (m.heads / m.kv_heads);
+                const uint32_t bytes = static_cast<uint32_t>(pos * m.dim * sizeof(float));
+                const int64_t base = (int64_t)kvh * m.capacity * m.dim;
+                for (uint32_t off = 0; off < bytes; off += 65536u) {
+                    const uint32_t len = min(65536u, bytes - off);
+                    bulk_prefetch_l2(reinterpret_cast<const uint8_t*>(nx.k_cache + base) + off, len);
+                    bulk_prefetch_l2(reinterpret_cast<const uint8_t*>(nx.v_cache + base) + off, len);
+                }
+            }
+        }
         const OpGeometry g = geometry(op);
         if (g.nblocks == 0) continue;
         // Row scales of this warp's row blocks, one lane per block, loaded
@@ -502,10 +554,30 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
             }
             consumer_sync();
             if (*abort_flag) return;
-            const float sq = sum_squares_sequential_order<kNC>(h, static_cast<int>(op.cols), sum_scratch, tid,
-                                                               [] { consumer_sync(); });
+            // Sum of squares left to right (one thread; squares and loads run
+            // ahead of the dependent additions).
+            if (tid == 0) {
+                const float4* h4 = reinterpret_cast<const float4*>(h);
+                float sq = 0.0f;
+                for (int64_t c = 0; c < vecs; c += 8) {
+                    float4 v[8];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) v[u] = c + u < vecs ? h4[c + u] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) {
+                        if (c + u < vecs) {
+                            sq = __fadd_rn(sq, __fmul_rn(v[u].x, v[u].x));
+                            sq = __fadd_rn(sq, __fmul_rn(v[u].y, v[u].y));
+                            sq = __fadd_rn(sq, __fmul_rn(v[u].z, v[u].z));
+                            sq = __fadd_rn(sq, __fmul_rn(v[u].w, v[u].w));
+                        }
+                    }
+                }
+                *total_s = sq;
+            }
+            consumer_sync();
             const float scale =
-                __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sq, static_cast<float>(op.cols)), m.epsilon)));
+                __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(*total_s, static_cast<float>(op.cols)), m.epsilon)));
 #pragma unroll
             for (int k = 0; k < kXVec; ++k) {
                 const int64_t i = tid + (int64_t)k * kNC;
@@ -706,12 +778,12 @@ int leafq_model_plan_create(const leafq_model_desc* d, leafq_model_plan_t** out)
     const int64_t h = d->hidden, f = d->intermediate, dim = d->head_dim;
     const int64_t qkv_rows = (int64_t)(d->heads + 2 * d->kv_heads) * dim;
     if (h <= 0 || f <= 0 || d->heads <= 0 || d->kv_heads <= 0 || d->heads % d->kv_heads ||
-        d->heads * dim != h || dim % 2 || dim > kMaxDim || d->vocab <= 0 || d->capacity <= 0 ||
+        d->heads * dim != h || dim % 4 || dim > kMaxDim || d->vocab <= 0 || d->capacity <= 0 ||
         d->capacity > kMaxCapacity || h > kScratchFloats || h % 16 || f % 16 || f > kMaxCols ||
         h > kMaxCols || 5 * d->layers + 1 > kMaxOps || d->heads > sm_count() ||
         !(d->attn_scale > 0.0f)) {
         set_error("leafq_model_plan_create: unsupported geometry (hidden and intermediate multiples of "
-                  "16 and <= 4096 / 8192, heads * head_dim == hidden, head_dim even and <= 256, "
+                  "16 and <= 4096 / 8192, heads * head_dim == hidden, head_dim a multiple of 4 and <= 256, "
                   "capacity <= 2048, heads <= SMs)");
         return LEAFQ_ERR_UNSUPPORTED;
     }

@@ -233,26 +233,30 @@ __device__ float sum_squares_sequential_order(const float* x, int n, SumScratch*
         SumStep prefix = sum_step_identity();
         for (int w = 0; w < warp; ++w) prefix = sum_step_then(prefix, sc->warp_total[w]);
         prefix = sum_step_then(prefix, lane_excl);
-        // Partial sums of this thread's elements; the first that leaves the binade.
+        // Partial sums of this thread's elements; the first that leaves the
+        // binade.  Partial sums only grow, so exactly one thread -- the one
+        // whose own prefix is still inside the binade -- finds it.
         int mb = sat_add(m, par0 ? prefix.inc1 : prefix.inc0);
         int par = par0 ? prefix.out1 : prefix.out0;
         int my_c = n, my_m = 0;
+        if (mb < (1 << 24)) {
 #pragma unroll
-        for (int j = 0; j < kPer; ++j) {
-            const int i = tid * per + j;
-            if (j < per && i >= i0 && i < n && my_c == n) {
-                const SumStep t = sum_step_of(p[j], e);
-                const int inc = par ? t.inc1 : t.inc0;
-                if (mb + inc >= (1 << 24)) {
-                    my_c = i;
-                    my_m = mb;
-                } else {
-                    mb += inc;
-                    par = par ? t.out1 : t.out0;
+            for (int j = 0; j < kPer; ++j) {
+                const int i = tid * per + j;
+                if (j < per && i >= i0 && i < n && my_c == n) {
+                    const SumStep t = sum_step_of(p[j], e);
+                    const int inc = par ? t.inc1 : t.inc0;
+                    if (mb + inc >= (1 << 24)) {
+                        my_c = i;
+                        my_m = mb;
+                    } else {
+                        mb += inc;
+                        par = par ? t.out1 : t.out0;
+                    }
                 }
             }
         }
-        if (my_c < n) atomicMin(&sc->crossing, my_c);
+        if (my_c < n) sc->crossing = my_c;
         const bool last_owner = (n - 1) / per == tid;
         sync();
         const int c = sc->crossing;

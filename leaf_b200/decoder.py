@@ -37,26 +37,41 @@ def _stream() -> int:
     return torch.cuda.current_stream().cuda_stream
 
 
-def _concat_rows(parts: list[HostTensor], interleave: bool = False) -> tuple:
-    """Rows of several equally quantised matrices as one: stacked (q | k | v)
-    or, with interleave, alternating (gate_0, up_0, gate_1, up_1, ...)."""
+def _on(a, device: torch.device) -> torch.Tensor:
+    """A payload (numpy view of the mapped artifact, or a tensor) on the device."""
+    if isinstance(a, torch.Tensor):
+        return a.to(device)
+    return torch.from_numpy(np.array(a)).to(device)
+
+
+def _concat_rows(parts: list[HostTensor], device: torch.device, interleave: bool = False) -> QuantWeight:
+    """Rows of several equally quantised matrices as one weight: stacked
+    (q | k | v) or, with interleave, alternating (gate_0, up_0, gate_1, ...)."""
     bits, group, cols = parts[0].bits, parts[0].group, parts[0].cols
     if any(p.bits != bits or p.group != group or p.cols != cols for p in parts):
         raise LeafError(_lib.LEAFQ_ERR_UNSUPPORTED, "fused projections need one precision and group")
+    datas = [_on(p.data, device) for p in parts]
+    scales = None if bits == 32 else [_on(p.scales, device) for p in parts]
     if interleave:
-        data = np.stack([np.asarray(p.data) for p in parts], axis=1).reshape(-1, parts[0].data.shape[1])
-        scales = (None if bits == 32 else
-                  np.stack([np.asarray(p.scales) for p in parts], axis=1).reshape(-1, parts[0].scales.shape[1]))
+        data = torch.stack(datas, dim=1).reshape(-1, datas[0].shape[1])
+        scales = None if scales is None else torch.stack(scales, dim=1).reshape(-1, scales[0].shape[1])
     else:
-        data = np.concatenate([np.asarray(p.data) for p in parts], axis=0)
-        scales = None if bits == 32 else np.concatenate([np.asarray(p.scales) for p in parts], axis=0)
-    return data, scales, sum(p.rows for p in parts), cols, bits, group
+        data = torch.cat(datas, dim=0)
+        scales = None if scales is None else torch.cat(scales, dim=0)
+    rows = sum(p.rows for p in parts)
+    w = QuantWeight(data.contiguous(), None if scales is None else scales.contiguous(), rows, cols, bits,
+                    group if bits != 32 else 0)
+    w.check()
+    return w
 
 
 class Decoder:
     def __init__(self, artifact, activation_bits: int = 8, device="cuda",
                  capacity: Optional[int] = None):
-        art = artifact if isinstance(artifact, Artifact) else Artifact(artifact)
+        """artifact: a path, an ``Artifact``, or any object with the same
+        ``config`` / ``get(name)`` interface whose payloads are tensors
+        (``leaf_b200.stack.random_decoder_model``)."""
+        art = artifact if hasattr(artifact, "get") else Artifact(artifact)
         cfg = art.config
         if not (cfg.norm_kind == 0 and cfg.position_kind == 0 and cfg.gated == 1 and
                 cfg.activation == 0 and cfg.parallel == 0 and cfg.sliding_window == 0 and
@@ -74,18 +89,14 @@ class Decoder:
         dev = self.device
 
         def f32(t: HostTensor):
-            return torch.from_numpy(np.array(t.data, dtype=np.float32).reshape(-1)).to(dev)
+            return _on(t.data, dev).to(torch.float32).reshape(-1).contiguous()
 
         def weight(parts, interleave=False):
-            data, scales, rows, cols, bits, group = _concat_rows(parts, interleave)
-            w = QuantWeight.from_host(data, scales, rows, cols, bits, group, device=dev)
-            w.check()
-            return w
+            return _concat_rows(parts, dev, interleave)
 
         emb = art.get("model.embed_tokens.weight")
-        self.embed_table = torch.from_numpy(np.array(emb.data)).to(dev)
-        self.embed_scales = (None if emb.scales is None else
-                             torch.from_numpy(np.array(emb.scales)).to(dev))
+        self.embed_table = _on(emb.data, dev).contiguous()
+        self.embed_scales = None if emb.scales is None else _on(emb.scales, dev).contiguous()
         self.embed_bits, self.embed_group = emb.bits, emb.group
         self.layers = []
         for i in range(cfg.layers):

@@ -18,6 +18,7 @@ from __future__ import annotations
 
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 
 from ._lib import LEAFQ_FLAG_PDL
@@ -181,3 +182,77 @@ class LinearStack:
             self.capture()
         self.graph.replay()
         return self.logits
+
+
+class _DeviceTensor:
+    """One tensor of a device-resident model in artifact layout."""
+
+    def __init__(self, name, rows, cols, bits, group, data, scales):
+        self.name, self.rows, self.cols, self.bits, self.group = name, rows, cols, bits, group
+        self.data, self.scales = data, scales
+
+
+class RandomDecoderModel:
+    """A Llama-shaped W8A8 decoder with random weights generated on the GPU,
+    with the ``config`` / ``get(name)`` interface of ``leaf_b200.artifact.Artifact``:
+    weights N(0, 0.02) quantised per row by the exporter's formula
+    (tools/export_decoder.py:91-105), embedding and lm_head per-row INT8,
+    RMSNorm weights 1, no EOS."""
+
+    def __init__(self, shape: StackShape, seed: int = 0, max_positions: int = 2048, device="cuda"):
+        from .artifact import DecoderConfig
+
+        h, f, heads, kv = shape.hidden, shape.intermediate, shape.heads, shape.kv_heads
+        d = h // heads
+        self.config = DecoderConfig(h, f, heads, kv, shape.layers, shape.vocab, max_positions,
+                                    0xFFFFFFFF, d, 0, 10000.0, float(np.float32(1e-5)), 0, 0, 0, 1, 0, d,
+                                    0, 1, 1.0)
+        gen = torch.Generator(device=device)
+        gen.manual_seed(seed)
+        self._tensors = {}
+
+        def mat(name, rows, cols):
+            w = random_w8_weight(rows, cols, gen, device)
+            self._tensors[name] = _DeviceTensor(name, rows, cols, 8, cols, w.data, w.scales.reshape(rows, 1))
+
+        def norm(name):
+            self._tensors[name] = _DeviceTensor(name, 1, h, 32, 0,
+                                                torch.ones((1, h), dtype=torch.float32, device=device), None)
+
+        mat("model.embed_tokens.weight", shape.vocab, h)
+        mat("lm_head.weight", shape.vocab, h)
+        norm("model.norm.weight")
+        for i in range(shape.layers):
+            p = f"model.layers.{i}."
+            norm(p + "input_layernorm.weight")
+            norm(p + "post_attention_layernorm.weight")
+            mat(p + "self_attn.q_proj.weight", heads * d, h)
+            mat(p + "self_attn.k_proj.weight", kv * d, h)
+            mat(p + "self_attn.v_proj.weight", kv * d, h)
+            mat(p + "self_attn.o_proj.weight", h, heads * d)
+            mat(p + "mlp.gate_proj.weight", f, h)
+            mat(p + "mlp.up_proj.weight", f, h)
+            mat(p + "mlp.down_proj.weight", h, f)
+
+    def get(self, name):
+        return self._tensors.get(name)
+
+    def release(self) -> None:
+        """Drop the per-matrix copies once a Decoder has fused them."""
+        self._tensors.clear()
+
+
+def decoder_step_bytes(shape: StackShape, position: int) -> int:
+    """Algorithmic HBM bytes of one whole-model decode step at cache length
+    `position`: every INT8 weight and row scale once, the embedding row, the
+    norm weights, the cached keys and values read (positions 0..position-1)
+    and this token's written, the hand-off vectors and the logits."""
+    h, f, heads, kv, layers = shape.hidden, shape.intermediate, shape.heads, shape.kv_heads, shape.layers
+    d = h // heads
+    layer, head = shape.linears()
+    weights = layers * sum(r * c + 4 * r for _, r, c in layer) + head[1] * (head[2] + 4)
+    embed = h + 4
+    norms = 4 * h * (2 * layers + 1)
+    kv_bytes = layers * 2 * kv * d * 4 * (position + 1)
+    handoff = layers * 8 * (shape.qkv_rows + h + h + f + h)
+    return weights + embed + norms + kv_bytes + handoff + 4 * shape.vocab
