@@ -1,18 +1,23 @@
 #!/usr/bin/env python
 """W8A8 decode tokens/s (TinyLlama-1.1B shape) + GEMV HBM GB/s vs peak.
 
-One step = one decode token through every W8A8 Linear of a TinyLlama-1.1B
-shaped decoder (22 layers x [q|k|v, o, gate|up, down] + lm_head, batch 1,
-1.04 GB of INT8 weights, inputs larger than L2), replayed as a CUDA graph
-holding one persistent leafq decode launch (leafq_decode_plan_run).  With
---gpus N each rank runs its own replica (an independent request stream);
-value is the sum over ranks.
+One step = one greedy decode token of a whole TinyLlama-1.1B-shaped W8A8
+decoder (config 3: 22 layers, hidden 2048, 32 query / 4 KV heads, SwiGLU
+5632, RMSNorm, RoPE, vocab 32000; random-init per-row INT8 weights, batch 1)
+after a 128-token random prompt: embedding, every layer's norms, q|k|v,
+RoPE, KV append, attention over the cache, o, gate|up, SiLU, down,
+residuals, final norm, lm_head and the argmax -- one launch of the
+whole-model kernel (leafq_model_plan_run), bit-identical to the reference
+decoder.  Decode positions 128..255 (the 128 generated tokens of config 3),
+repeated for K steps; 1.04 GB of weights streamed per step (larger than L2).
+With --gpus N each rank decodes its own request stream (data-parallel
+replicas); value is the sum over ranks.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 Prints one JSON line (rank 0).  --impl reference times the reference's own
-CPU kernels (oracle/_ref, compiled from the reference sources) on the host
-cores for the same metric and workload.
+CPU decoder (oracle/_ref/leaf_decoder, compiled from the reference sources)
+on the host cores for the same metric and workload shape.
 """
 from __future__ import annotations
 
@@ -38,11 +43,11 @@ FALLBACK_HBM_GBS = 6650.0
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=200)
-    p.add_argument("--warmup", type=int, default=10)
+    p.add_argument("--steps", type=int, default=254)
+    p.add_argument("--warmup", type=int, default=8)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    p.add_argument("--cpu-seconds", type=float, default=12.0,
-                   help="bounded CPU-baseline sample (rank 0, N=1)")
+    p.add_argument("--cpu-tokens", type=int, default=32,
+                   help="tokens the bounded CPU-baseline sample generates (rank 0, N=1)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--case", choices=sorted(CASES),
                    help="run one small single-kernel case three times and exit (for ncu captures)")
@@ -74,6 +79,7 @@ CASES = {
     "gemm_big": (4096, 5632, 2048, 8, 2048, 8),  # large-M prefill
     "w4": (1, 11008, 4096, 4, 32, 32),          # config 1 INT4 weight-only GEMV
     "decode_small": None,                        # persistent decode kernel, 3-layer stack
+    "model_small": None,                         # whole-model decode kernel, 3-layer model
 }
 
 
@@ -82,6 +88,26 @@ def run_case(name):
 
     import leaf_b200 as lq
 
+    if name == "model_small":
+        # The whole-model decode kernel on a 3-layer TinyLlama-width model
+        # (198 MB of weights: larger than L2, small enough for ncu replays).
+        from leaf_b200.decoder import Decoder
+        from leaf_b200.stack import RandomDecoderModel, StackShape
+
+        torch.cuda.set_device(0)
+        model = RandomDecoderModel(StackShape(layers=3), seed=5)
+        dec = Decoder(model)
+        model.release()
+        dec.build_fused()
+        dec.forward(list(range(1, 129)))
+        for _ in range(3):
+            dec.step_fused()
+        torch.cuda.synchronize()
+        if dec.device_status() != 0:
+            raise RuntimeError("device status not ok")
+        print(json.dumps({"case": name, "layers": 3, "status": "ok"}))
+        dec.close()
+        return
     if name == "decode_small":
         # The persistent decode kernel on a 3-layer TinyLlama-width stack
         # (132 MB of weights: larger than L2, small enough for ncu replays).
@@ -121,78 +147,58 @@ def measured_peaks():
     return FALLBACK_HBM_GBS, "fallback"
 
 
+PROMPT = 128   # config 3: 128 random prompt ids, then 128 greedy tokens
+GENERATED = 128
+
+
 def workload_config(n_gpus):
     return {
-        "workload": "tinyllama-1.1b w8a8 decode linear stack: 22 x [qkv 2560x2048, o 2048x2048, "
-                    "gate_up 11264x2048, down 2048x5632] + lm_head 32000x2048, batch 1 per GPU",
+        "workload": "tinyllama-1.1b w8a8 greedy decode, whole decoder per step (22 layers: RMSNorm, "
+                    "q|k|v, RoPE, KV cache, GQA attention, o, gate|up, SiLU, down, residuals; final "
+                    "norm, lm_head 32000x2048, argmax), 128-token prompt, positions 128..255, batch 1 "
+                    "per GPU",
         "model": "TinyLlama-1.1B shape (random-init INT8 per-row weights)",
         "global_batch": n_gpus,
-        "seq_len": 1,
+        "seq_len": PROMPT + GENERATED,
         "parallelism": f"replicas x{n_gpus}",
         "l2": "inputs larger than L2 (1.04 GB of weights streamed per step)",
     }
 
 
 # ----------------------------------------------------------------- CPU side
-def cpu_reference_stack(threads: int, seconds: float, steps: int = 0, warmup: int = 0):
-    """Times the reference's own CPU kernels (oracle/_ref) on one decode
-    token of the same stack (separate q, k, v, gate, up projections as the
-    reference calls them).  Returns (tokens_per_s, kind, sample text,
-    per-step seconds list)."""
+def cpu_reference_decoder(threads: int, new_tokens: int, warmup: int = 0):
+    """The reference's own CPU decoder (oracle/_ref/leaf_decoder built from
+    engine/src/decoder.cpp with leaf/cli.py's flags) on a TinyLlama-shaped
+    W8A8 artifact (seeded random weights written by oracle/fixture.py in the
+    reference's export format), 128-token prompt, activation bits 8.
+    Returns (decode tokens/s, sample text)."""
+    import tempfile
+
     import oracle
-    from leaf_b200.stack import StackShape
+    from oracle import fixture as fx
 
-    shape = StackShape()
-    kind = "reference" if oracle.ref_available() else "port"
-    rng = np.random.default_rng(7)
-    h, f, kv = shape.hidden, shape.intermediate, shape.kv_heads * shape.head_dim
-    names = [("q", h, h), ("k", kv, h), ("v", kv, h), ("o", h, h), ("gate", f, h), ("up", f, h),
-             ("down", h, f)]
-    # Two distinct layer copies (2 x 44 MB) cycle through the 22 layers so
-    # the weights are not cache-resident; lm_head is its own 65.5 MB.
-    layers = []
-    for _ in range(2):
-        layers.append({n: (rng.integers(-127, 128, (r, c), dtype=np.int8),
-                           (rng.random((r, 1), dtype=np.float32) * 1e-3 + 1e-4).astype(np.float32))
-                       for n, r, c in names})
-    head = (rng.integers(-127, 128, (shape.vocab, h), dtype=np.int8),
-            (rng.random((shape.vocab, 1), dtype=np.float32) * 1e-3 + 1e-4).astype(np.float32))
-    x0 = rng.standard_normal((1, h)).astype(np.float32)
-
-    def run(w, x, n):
-        if kind == "reference":
-            return oracle.ref_linear_int(x, w[0], w[1], 8, w[0].shape[1], None, threads=threads, mode=0)
-        return oracle.linear_int(x, w[0], w[1], 8, w[0].shape[1], None)
-
-    def token():
-        x = x0
-        for i in range(shape.layers):
-            L = layers[i % 2]
-            q = run(L["q"], x, "q")
-            run(L["k"], x, "k")
-            run(L["v"], x, "v")
-            o = run(L["o"], q, "o")
-            run(L["gate"], o, "gate")
-            up = run(L["up"], o, "up")
-            x = run(L["down"], up, "down")
-        return run(head, x, "lm_head")
-
-    for _ in range(max(warmup, 1)):
-        token()
-    times = []
-    start = time.perf_counter()
-    while True:
-        t0 = time.perf_counter()
-        token()
-        times.append(time.perf_counter() - t0)
-        if steps and len(times) >= steps:
-            break
-        if not steps and time.perf_counter() - start >= seconds:
-            break
-    per = float(np.mean(times))
-    sample = (f"{len(times)} decode tokens of the full 22-layer stack + lm_head (2 distinct layer "
-              f"weight copies cycled), {threads} threads, reference Workers grain 32")
-    return 1.0 / per, kind, sample, times
+    if not oracle.REF_DECODER.exists():
+        raise RuntimeError("oracle/_ref/leaf_decoder is not built")
+    with tempfile.TemporaryDirectory() as tmp:
+        work = Path(tmp)
+        art = work / "tinyllama_w8.leaf"
+        fx.write_artifact(art, fx.TINYLLAMA, fx.llama_tensors(fx.TINYLLAMA, 7, 0.0), 8, 64)
+        ids = fx.prompt_ids(fx.TINYLLAMA, 3, PROMPT)
+        with (work / "tokens.bin").open("wb") as f:
+            f.write(np.asarray([1, len(ids)], dtype="<u4").tobytes())
+            f.write(np.asarray(ids, dtype="<u4").tobytes())
+        cmd = [str(oracle.REF_DECODER), str(art), str(work / "tokens.bin"), str(work / "logits.bin"),
+               str(work / "metrics.json"), "bench-generate", str(threads), "1", str(warmup),
+               str(new_tokens), "0", "1", "8"]
+        subprocess.run(cmd, check=True, capture_output=True, text=True)
+        metrics = json.loads((work / "metrics.json").read_text())
+    steps = metrics.get("decode_samples_ms") or []
+    if not steps:
+        raise RuntimeError("reference decoder reported no decode steps")
+    per_ms = float(np.mean(steps))
+    sample = (f"{len(steps)} greedy decode steps (positions {PROMPT}..{PROMPT + len(steps) - 1}) of the "
+              f"reference decoder bench-generate on a TinyLlama-shape W8A8 artifact, {threads} threads")
+    return 1000.0 / per_ms, sample
 
 
 # ----------------------------------------------------------------- clocks
@@ -245,21 +251,18 @@ def run_reference(args, rank, world):
     if rank != 0:
         return
     threads = max(1, min(os.cpu_count() or 1, 64))
+    new_tokens = max(2, min(args.steps + 1, GENERATED))
     try:
-        import oracle
-        if not oracle.ref_available():
-            oracle.build()
+        value, sample = cpu_reference_decoder(threads, new_tokens, warmup=min(args.warmup, 1))
     except Exception as exc:  # noqa: BLE001
-        print(json.dumps({"impl": "reference", "unavailable": f"CPU reference kernels missing: {exc}"}))
+        print(json.dumps({"impl": "reference", "unavailable": f"reference CPU decoder failed: {exc}"}))
         return
-    value, kind, sample, times = cpu_reference_stack(threads, 0.0, steps=args.steps, warmup=args.warmup)
-    ms = 1000.0 * float(np.mean(times))
     line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "int8", "data": "synthetic", "impl": "reference",
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": new_tokens - 1,
+        "warmup": args.warmup, "ms_per_step": 1000.0 / value, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic", "impl": "reference",
         "config": workload_config(1),
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind,
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference",
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -271,27 +274,42 @@ def run_ours(args, rank, world, local_rank):
     import torch.distributed as dist
 
     import leaf_b200 as lq
-    from leaf_b200.stack import LinearStack
+    from leaf_b200._lib import check
+    from leaf_b200.decoder import Decoder
+    from leaf_b200.stack import RandomDecoderModel, StackShape, decoder_step_bytes
 
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
-    stack = LinearStack(tokens=1, seed=1234 + rank, device=device)
-    # Reference point: the same step as one leafq_linear launch per linear
-    # (89 launches, programmatic dependent launch), CUDA events, 20 replays.
-    stack.capture(pdl=True)
-    for _ in range(3):
-        stack.graph.replay()
-    p_start, p_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    p_start.record()
-    for _ in range(20):
-        stack.graph.replay()
-    p_end.record()
-    torch.cuda.synchronize(device)
-    per_linear_ms = p_start.elapsed_time(p_end) / 20
-    # The measured path: the whole step as one persistent launch.
-    stack.capture_persistent()
-    launches = stack.launches_per_step(persistent=True)
-    step_bytes = stack.shape.step_bytes(1)
+    shape = StackShape()
+    model = RandomDecoderModel(shape, seed=1234 + rank, device=device)
+    dec = Decoder(model, device=device)
+    model.release()
+    del model
+    dec.build_fused()
+    lib = lq.load()
+    stream = torch.cuda.current_stream(device)
+    gen = torch.Generator().manual_seed(99 + rank)
+    prompt = torch.randint(0, shape.vocab, (PROMPT,), generator=gen).tolist()
+
+    # Prefill the prompt (per-operator path), first token by argmax.
+    logits = dec.forward(prompt)
+    check(lib.leafq_argmax(stream.cuda_stream, logits.data_ptr(), 1, shape.vocab, dec.token.data_ptr()))
+    first = dec.token.clone()
+
+    def rewind():
+        """Back to the state right after the prompt: the next step decodes
+        position 128 again (cache rows >= 128 are rewritten)."""
+        dec.position.fill_(PROMPT)
+        dec.token.copy_(first)
+
+    def steps_device(k):
+        done = 0
+        while done < k:
+            rewind()
+            r = min(GENERATED - 1, k - done)
+            for _ in range(r):
+                dec.step_fused()
+            done += r
 
     def barrier():
         if world > 1:
@@ -304,10 +322,25 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    stream = torch.cuda.current_stream(device)
-    for _ in range(max(args.warmup, 3)):
-        stack.replay()
+    # Reference point: the same decode step as per-operator kernels replayed
+    # from one CUDA graph (about 200 launches per token).
+    dec.capture_decode()
+    rewind()
+    for _ in range(3):
+        dec.graph.replay()
+    rewind()
+    g_start, g_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g_start.record(stream)
+    for _ in range(GENERATED - 1):
+        dec.graph.replay()
+    g_end.record(stream)
     torch.cuda.synchronize(device)
+    per_op_us = g_start.elapsed_time(g_end) * 1000.0 / (GENERATED - 1)
+
+    steps_device(max(args.warmup, 3))
+    torch.cuda.synchronize(device)
+    if lib.leafq_device_status() != 0:
+        raise RuntimeError(f"device status: {lib.leafq_last_error().decode()}")
 
     out_dir = REPO / "gpurun_out"
     out_dir.mkdir(exist_ok=True)
@@ -320,37 +353,51 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize(device)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record(stream)
-    for _ in range(args.steps):
-        stack.graph.replay()
+    steps_device(args.steps)
     end.record(stream)
     torch.cuda.synchronize(device)
     barrier()
     ms_total = max_over_ranks(start.elapsed_time(end))
-    # ------------------------------------------------ end to end (host buffers)
-    x_host = torch.randn(stack.x.shape, dtype=torch.float32).pin_memory()
-    logits_host = torch.empty(stack.logits.shape, dtype=torch.float32).pin_memory()
+    # ------------------------------------------------ end to end (host tokens)
+    # A streaming loop: every step copies its input token from pinned host
+    # memory, runs, and copies the produced token back to the host (and
+    # waits for it, as a server streaming tokens does).
+    tok_in = torch.empty(1, dtype=torch.int32).pin_memory()
+    tok_out = torch.empty(1, dtype=torch.int32).pin_memory()
+    tok_in.copy_(first.cpu())
     barrier()
     torch.cuda.synchronize(device)
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_start.record(stream)
-    for _ in range(args.steps):
-        stack.x.copy_(x_host, non_blocking=True)
-        stack.graph.replay()
-        logits_host.copy_(stack.logits, non_blocking=True)
+    done = 0
+    while done < args.steps:
+        dec.position.fill_(PROMPT)
+        tok_in.copy_(first.cpu())
+        r = min(GENERATED - 1, args.steps - done)
+        for _ in range(r):
+            dec.token.copy_(tok_in, non_blocking=True)
+            dec.step_fused()
+            tok_out.copy_(dec.token, non_blocking=True)
+            stream.synchronize()
+            tok_in.copy_(tok_out)
+        done += r
     e_end.record(stream)
     torch.cuda.synchronize(device)
     barrier()
     e2e_ms_total = max_over_ranks(e_start.elapsed_time(e_end))
     time.sleep(0.2)
     clocks = sampler.stop()
-    status = lq.load().leafq_device_status()
+    status = lib.leafq_device_status()
     if status != 0:
-        raise RuntimeError(f"device status {status}: {lq.load().leafq_last_error().decode()}")
+        raise RuntimeError(f"device status {status}: {lib.leafq_last_error().decode()}")
+    dec.close()
 
     ms_step = ms_total / args.steps
     value = world * 1000.0 / ms_step
     e2e_ms_step = e2e_ms_total / args.steps
     peak, peak_kind = measured_peaks()
+    positions = [PROMPT + (i % (GENERATED - 1)) for i in range(args.steps)]
+    step_bytes = float(np.mean([decoder_step_bytes(shape, p) for p in positions]))
     achieved = step_bytes / (ms_step * 1e-3) / 1e9
     traffic = read_traffic()
 
@@ -358,8 +405,8 @@ def run_ours(args, rank, world, local_rank):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = max(1, min(os.cpu_count() or 1, 64))
         try:
-            cpu_value, kind, sample, _ = cpu_reference_stack(threads, args.cpu_seconds)
-            cpu = {"value": cpu_value, "unit": UNIT, "cores": threads, "kind": kind, "sample": sample}
+            cpu_value, sample = cpu_reference_decoder(threads, args.cpu_tokens)
+            cpu = {"value": cpu_value, "unit": UNIT, "cores": threads, "kind": "reference", "sample": sample}
         except Exception as exc:  # noqa: BLE001
             cpu = {"value": None, "unit": UNIT, "cores": threads, "kind": "reference",
                    "sample": f"failed: {exc}"}
@@ -373,17 +420,17 @@ def run_ours(args, rank, world, local_rank):
             "roofline": {
                 "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "traffic": traffic,
-                "kernel": "decode_persistent_kernel (the step's only kernel; one launch per step)",
+                "kernel": "decode_model_kernel (the step's only kernel; one launch per token)",
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                 else "fallback 6650 GB/s",
                 "algorithmic_bytes_per_step": step_bytes,
             },
             "e2e": {"value": world * 1000.0 / e2e_ms_step, "unit": UNIT,
-                    "h2d_bytes_per_step": int(stack.x.numel() * 4),
-                    "d2h_bytes_per_step": int(stack.logits.numel() * 4),
+                    "h2d_bytes_per_step": int(tok_in.numel() * 4),
+                    "d2h_bytes_per_step": int(tok_out.numel() * 4),
                     "ms_per_step": e2e_ms_step},
-            "gpu_launches": launches * args.steps,
-            "per_linear_launch_ms_per_step": per_linear_ms,
+            "gpu_launches": args.steps,
+            "per_operator_graph_us_per_token": per_op_us,
             "clocks": clocks,
             "cpu_baseline": cpu,
             "when": datetime.datetime.now(datetime.timezone.utc).isoformat(timespec="seconds"),
@@ -393,7 +440,7 @@ def run_ours(args, rank, world, local_rank):
 
 def read_traffic():
     """DRAM bytes per decode step from the committed ncu summary, if any."""
-    path = REPO / "profiles" / "decode_persistent_tinyllama_step.md"
+    path = REPO / "profiles" / "decode_model_tinyllama_step.md"
     if not path.exists():
         return None
     for line in path.read_text().splitlines():

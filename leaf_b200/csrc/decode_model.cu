@@ -534,7 +534,6 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
             }
         } else {
             // RMSNorm of the hidden vector (norm(), decoder.cpp:706-727).
-            float* h = scratch;
             if (op.xsrc == kXNormEmbed) {
 #pragma unroll
                 for (int k = 0; k < kXVec; ++k) {
@@ -547,34 +546,20 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
                 ok = false;
                 *abort_flag = 1;
             }
+            // Squares in parallel; then one thread adds them left to right
+            // (the additions are the only dependent chain).
+            float* sq4 = scratch;
 #pragma unroll
             for (int k = 0; k < kXVec; ++k) {
                 const int64_t i = tid + (int64_t)k * kNC;
-                if (i < vecs) reinterpret_cast<float4*>(h)[i] = xr[k];
+                if (i < vecs)
+                    reinterpret_cast<float4*>(sq4)[i] =
+                        make_float4(__fmul_rn(xr[k].x, xr[k].x), __fmul_rn(xr[k].y, xr[k].y),
+                                    __fmul_rn(xr[k].z, xr[k].z), __fmul_rn(xr[k].w, xr[k].w));
             }
             consumer_sync();
             if (*abort_flag) return;
-            // Sum of squares left to right (one thread; squares and loads run
-            // ahead of the dependent additions).
-            if (tid == 0) {
-                const float4* h4 = reinterpret_cast<const float4*>(h);
-                float sq = 0.0f;
-                for (int64_t c = 0; c < vecs; c += 8) {
-                    float4 v[8];
-#pragma unroll
-                    for (int u = 0; u < 8; ++u) v[u] = c + u < vecs ? h4[c + u] : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-                    for (int u = 0; u < 8; ++u) {
-                        if (c + u < vecs) {
-                            sq = __fadd_rn(sq, __fmul_rn(v[u].x, v[u].x));
-                            sq = __fadd_rn(sq, __fmul_rn(v[u].y, v[u].y));
-                            sq = __fadd_rn(sq, __fmul_rn(v[u].z, v[u].z));
-                            sq = __fadd_rn(sq, __fmul_rn(v[u].w, v[u].w));
-                        }
-                    }
-                }
-                *total_s = sq;
-            }
+            if (tid == 0) *total_s = sum_in_order(sq4, static_cast<int>(op.cols));
             consumer_sync();
             const float scale =
                 __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(*total_s, static_cast<float>(op.cols)), m.epsilon)));

@@ -104,7 +104,6 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(
     extern __shared__ float row[];  // [width] values, then [width] squares
     float* squares = row + width;
     __shared__ float total;
-    __shared__ SumScratch sum_scratch;
     const int64_t t = blockIdx.x;
     float* h = hidden + t * width;
     for (int64_t c = threadIdx.x; c < width; c += blockDim.x) {
@@ -119,14 +118,14 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(
         squares[c] = __fmul_rn(v, v);
     }
     __syncthreads();
-    if (width <= 8 * kNormThreads) {
-        const float sq = sum_squares_sequential_order<kNormThreads>(
-            row, static_cast<int>(width), &sum_scratch, static_cast<int>(threadIdx.x), [] { __syncthreads(); });
-        if (threadIdx.x == 0) total = sq;
-    } else if (threadIdx.x == 0) {
-        float sq = 0.0f;
-        for (int64_t c = 0; c < width; ++c) sq = __fadd_rn(sq, squares[c]);
-        total = sq;
+    if (threadIdx.x == 0) {
+        if ((width & 3) == 0) {
+            total = sum_in_order(squares, static_cast<int>(width));
+        } else {
+            float sq = 0.0f;
+            for (int64_t c = 0; c < width; ++c) sq = __fadd_rn(sq, squares[c]);
+            total = sq;
+        }
     }
     __syncthreads();
     const float scale =

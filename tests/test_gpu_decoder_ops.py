@@ -1,6 +1,7 @@
 """Decoder operators through the C ABI against the CPU restatement
 (oracle/decoder.py, itself bit-exact against the reference decoder):
-RMSNorm (block-parallel sum in the reference's sequential rounding), RoPE +
+RMSNorm (sum of squares in the reference's left-to-right order, on inputs
+built to stress rounding: ties, zeros, subnormal squares, overflow), RoPE +
 KV append, attention and the SiLU gate, bit for bit."""
 import ctypes
 
@@ -40,7 +41,7 @@ def _vectors(rng, kind, rows, width):
     raise ValueError(kind)
 
 
-@pytest.mark.parametrize("width", [64, 100, 2048, 3000])
+@pytest.mark.parametrize("width", [64, 100, 102, 2048, 3000])
 @pytest.mark.parametrize("kind", ["normal", "outliers", "grid", "zeros", "tiny", "huge", "pow2"])
 def test_rmsnorm_bit_exact(cuda_device, kind, width):
     rng = np.random.default_rng(hash((kind, width)) % 2**32)
