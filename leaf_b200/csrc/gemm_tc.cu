@@ -8,8 +8,10 @@
 // int32 dot product of every (token, row), and the same epilogue:
 //   y = fma(float(acc) * sx[token], sw[row], 0.0f) + (bias[row] or 0.0f).
 //
-// Tiling: D[128 tokens, 256 rows] per tile (one UMMA of M=128, N=256, K=32
-// per instruction, four per 128-byte K block).  Operands are K-major: the
+// Tiling: D[128 tokens, BN rows] per tile (one UMMA of M=128, N=BN, K=32
+// per instruction, four per 128-byte K block); BN = 256, or 128 when the
+// 256-wide tiles would leave SMs idle (few tokens: prefill chunks of a few
+// hundred tokens), so that every SM gets a tile.  Operands are K-major: the
 // codes [tokens, cols] and the weights [rows, cols] are both row-major with
 // K contiguous, loaded by TMA with 128-byte swizzle into a 4-stage ring
 // (48 KB per stage).  Warp roles (192 threads, persistent over tiles):
@@ -31,16 +33,19 @@ namespace leafq {
 namespace {
 
 constexpr int BM = 128;
-constexpr int BN = 256;
 constexpr int BK = 128;  // bytes (= int8 elements) of K per stage
 constexpr int UMMA_K = 32;
-constexpr int kStages = 4;
 constexpr int kThreads = 192;
-constexpr int kAccCols = BN;      // TMEM columns per accumulator
-constexpr int kTmemCols = 2 * kAccCols;
 constexpr int kABytes = BM * BK;  // 16 KB
-constexpr int kBBytes = BN * BK;  // 32 KB
-constexpr size_t kSmemBytes = (size_t)kStages * (kABytes + kBBytes) + 1024 /*barriers*/ + 1024 /*align*/;
+
+template <int BN>
+struct TileCfg {
+    static constexpr int kStages = BN == 256 ? 4 : 6;
+    static constexpr int kAccCols = BN;  // TMEM columns per accumulator
+    static constexpr int kTmemCols = 2 * kAccCols;
+    static constexpr int kBBytes = BN * BK;
+    static constexpr size_t kSmemBytes = (size_t)kStages * (kABytes + kBBytes) + 1024 /*barriers*/ + 1024 /*align*/;
+};
 
 struct GemmArgs {
     const float* sx;
@@ -54,9 +59,14 @@ struct GemmArgs {
     int n_tiles;
 };
 
+template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_w8a8_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_w,
                     const GemmArgs a) {
+    constexpr int kStages = TileCfg<BN>::kStages;
+    constexpr int kAccCols = TileCfg<BN>::kAccCols;
+    constexpr int kTmemCols = TileCfg<BN>::kTmemCols;
+    constexpr int kBBytes = TileCfg<BN>::kBBytes;
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte alignment for the swizzled operand tiles.
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -259,16 +269,31 @@ bool gemm_tc_supported(int64_t tokens, int64_t cols, int64_t rows, int bits, int
     return bits == 8 && group == cols && cols % 16 == 0 && cols >= BK && aligned16(weight);
 }
 
-int launch_gemm_tc(cudaStream_t s, const int8_t* q, const float* sx, int64_t tokens, int64_t cols,
-                   const int8_t* weight, const float* wscales, int64_t rows, const float* bias,
-                   float* y, bool pdl) {
-    if (tokens == 0 || rows == 0) return LEAFQ_OK;
-    if (!aligned16(q) || !aligned16(weight) || cols % 16 != 0) return LEAFQ_ERR_UNSUPPORTED;
+namespace {
+template <int BN>
+int run_tiles(cudaStream_t s, const int8_t* q, const int8_t* weight, int64_t cols, int64_t tokens,
+              int64_t rows, GemmArgs a, bool pdl) {
     CUtensorMap map_q, map_w;
     int st = make_map(&map_q, q, cols, tokens, BM);
     if (st) return st;
     st = make_map(&map_w, weight, cols, rows, BN);
     if (st) return st;
+    a.n_tiles = static_cast<int>((rows + BN - 1) / BN);
+    const int64_t tiles = (int64_t)a.m_tiles * a.n_tiles;
+    const int grid = static_cast<int>(std::min<int64_t>(tiles, sm_count()));
+    constexpr size_t smem = TileCfg<BN>::kSmemBytes;
+    st = allow_smem(reinterpret_cast<const void*>(gemm_w8a8_tc_kernel<BN>), smem, "gemm_w8a8_tc");
+    if (st) return st;
+    return launch(gemm_w8a8_tc_kernel<BN>, dim3(grid), dim3(kThreads), smem, s, pdl, "gemm_w8a8_tc",
+                  map_q, map_w, a);
+}
+}  // namespace
+
+int launch_gemm_tc(cudaStream_t s, const int8_t* q, const float* sx, int64_t tokens, int64_t cols,
+                   const int8_t* weight, const float* wscales, int64_t rows, const float* bias,
+                   float* y, bool pdl) {
+    if (tokens == 0 || rows == 0) return LEAFQ_OK;
+    if (!aligned16(q) || !aligned16(weight) || cols % 16 != 0) return LEAFQ_ERR_UNSUPPORTED;
     GemmArgs a;
     a.sx = sx;
     a.ws = wscales;
@@ -278,13 +303,9 @@ int launch_gemm_tc(cudaStream_t s, const int8_t* q, const float* sx, int64_t tok
     a.rows = rows;
     a.cols = cols;
     a.m_tiles = static_cast<int>((tokens + BM - 1) / BM);
-    a.n_tiles = static_cast<int>((rows + BN - 1) / BN);
-    const int64_t tiles = (int64_t)a.m_tiles * a.n_tiles;
-    const int grid = static_cast<int>(std::min<int64_t>(tiles, sm_count()));
-    st = allow_smem(reinterpret_cast<const void*>(gemm_w8a8_tc_kernel), kSmemBytes, "gemm_w8a8_tc");
-    if (st) return st;
-    return launch(gemm_w8a8_tc_kernel, dim3(grid), dim3(kThreads), kSmemBytes, s, pdl,
-                  "gemm_w8a8_tc", map_q, map_w, a);
+    const int64_t wide_tiles = (int64_t)a.m_tiles * ((rows + 255) / 256);
+    if (wide_tiles >= sm_count()) return run_tiles<256>(s, q, weight, cols, tokens, rows, a, pdl);
+    return run_tiles<128>(s, q, weight, cols, tokens, rows, a, pdl);
 }
 
 }  // namespace leafq
