@@ -66,3 +66,53 @@ def test_zero_sized_calls_are_no_ops():
     lib = _lib.load()
     assert lib.leafq_linear(None, None, 0, 64, None, None, 8, 8, 64, 8, None, None, None, 0, 0) == 0
     assert lib.leafq_quantize_act(None, None, 0, 64, None, None) == 0
+
+
+def test_decoder_ops_reject_bad_shapes_on_host():
+    lib = _lib.load()
+    d = ctypes.c_void_p(16)
+    assert lib.leafq_rmsnorm(None, d, None, 0, 2, 0, d, 1e-5, d) == _lib.LEAFQ_ERR_INVALID
+    assert lib.leafq_rmsnorm(None, d, None, 0, 2, 20000, d, 1e-5, d) == _lib.LEAFQ_ERR_INVALID
+    assert lib.leafq_rotary_append(None, d, 1, 6, 4, 64, 64, d, d, d, d, d, d, 8) == _lib.LEAFQ_ERR_INVALID
+    assert lib.leafq_rotary_append(None, d, 1, 8, 2, 64, 65, d, d, d, d, d, d, 8) == _lib.LEAFQ_ERR_INVALID
+    assert lib.leafq_attention(None, d, d, d, 1, 8, 3, 64, d, 8, 0.5, d) == _lib.LEAFQ_ERR_INVALID
+    assert lib.leafq_attention(None, d, d, d, 1, 8, 2, 64, d, 8, 0.0, d) == _lib.LEAFQ_ERR_INVALID
+    assert lib.leafq_silu_gate(None, d, 1, 0, d) == _lib.LEAFQ_ERR_INVALID
+    assert lib.leafq_argmax(None, d, 1, 0, d) == _lib.LEAFQ_ERR_INVALID
+    assert lib.leafq_embed(None, d, 1, d, None, 8, 64, 10, 64, 1.0, d, None) == _lib.LEAFQ_ERR_INVALID
+    assert lib.leafq_advance_position(None, None, 1) == _lib.LEAFQ_ERR_INVALID
+    # Zero tokens are no-ops.
+    assert lib.leafq_silu_gate(None, None, 0, 8, None) == 0
+    assert lib.leafq_attention(None, None, None, None, 0, 8, 2, 64, None, 8, 0.5, None) == 0
+
+
+def test_rope_tables_match_libm_on_host():
+    import numpy as np
+
+    from oracle.decoder import rope_tables
+
+    lib = _lib.load()
+    cos = np.empty((40, 32), np.float32)
+    sin = np.empty_like(cos)
+    assert lib.leafq_rope_tables(ctypes.c_float(10000.0), 64, 40, cos.ctypes.data, sin.ctypes.data) == 0
+    c, s = rope_tables(10000.0, 64, 40)
+    assert np.array_equal(cos.view(np.uint32), c.view(np.uint32))
+    assert np.array_equal(sin.view(np.uint32), s.view(np.uint32))
+
+
+def test_plans_reject_bad_arguments_on_host():
+    lib = _lib.load()
+    out = ctypes.c_void_p()
+    handle = (ctypes.c_uint8 * _lib.LEAFQ_IPC_HANDLE_BYTES)()
+    assert lib.leafq_allgather_init(0, 9, 16, ctypes.byref(out), handle) == _lib.LEAFQ_ERR_INVALID
+    assert lib.leafq_allgather_init(2, 2, 16, ctypes.byref(out), handle) == _lib.LEAFQ_ERR_INVALID
+    assert lib.leafq_allgather_run(None, None, None, 1, 1, 0, 1, None) == _lib.LEAFQ_ERR_INVALID
+    assert lib.leafq_model_plan_create(None, ctypes.byref(out)) == _lib.LEAFQ_ERR_INVALID
+    desc = _lib.ModelDesc()
+    desc.layers = 1
+    desc.layer = ctypes.c_void_p(16)
+    desc.hidden, desc.intermediate, desc.heads, desc.kv_heads = 100, 256, 4, 2  # hidden % 16 != 0
+    desc.head_dim, desc.vocab, desc.capacity, desc.attn_scale = 25, 10, 8, 0.5
+    assert lib.leafq_model_plan_create(ctypes.byref(desc), ctypes.byref(out)) == _lib.LEAFQ_ERR_UNSUPPORTED
+    assert lib.leafq_model_plan_run(None, None) == _lib.LEAFQ_ERR_INVALID
+    assert lib.leafq_model_plan_destroy(None) == 0
