@@ -410,6 +410,13 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
                 }
             // scores[k] = (q.k * scale) * scale with q.k summed left to right.
             float local_max = -INFINITY;
+            if (tid == kNC - 1) {  // the current token's key (from shared memory), alongside
+                float dot = 0.0f;
+                for (int d = 0; d < dim; ++d) dot = __fadd_rn(dot, __fmul_rn(qs[d], ks[d]));
+                const float sc = __fmul_rn(__fmul_rn(dot, m.attn_scale), m.attn_scale);
+                scores[pos] = sc;
+                local_max = sc;
+            }
             for (int c = 0; c < nchunks; ++c) {
                 const int64_t k0 = (int64_t)c * chunk;
                 const int nk = static_cast<int>(min64(chunk, pos - k0));
@@ -435,13 +442,6 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
                     local_max = fmaxf(local_max, sc);
                 }
                 consumer_sync();  // chunk consumed
-            }
-            if (tid == kNC - 1) {  // the current token's key, from shared memory
-                float dot = 0.0f;
-                for (int d = 0; d < dim; ++d) dot = __fadd_rn(dot, __fmul_rn(qs[d], ks[d]));
-                const float sc = __fmul_rn(__fmul_rn(dot, m.attn_scale), m.attn_scale);
-                scores[pos] = sc;
-                local_max = fmaxf(local_max, sc);
             }
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) local_max = fmaxf(local_max, __shfl_xor_sync(0xffffffffu, local_max, o));
