@@ -315,6 +315,28 @@ int leafq_rotary_append(void* stream, const float* qkv, int64_t tokens, int head
 int leafq_attention(void* stream, const float* q_heads, const float* k_cache, const float* v_cache,
                     int64_t tokens, int heads, int kv_heads, int dim, const int32_t* position,
                     int64_t capacity, float scale, float* out);
+/* Batches of independent sequences (several requests decoded together).
+ * Sequence s owns rows s*tokens .. s*tokens+tokens-1 of qkv and out, the
+ * start position positions[s] (device int32 array), and its own caches at
+ * s * kv_heads * capacity * dim of k_cache / v_cache ([sequences][kv_heads]
+ * [capacity][dim]); q_heads is [sequences][heads][tokens][dim].  Every
+ * sequence's results equal the single-sequence calls' bit for bit.  A start
+ * position with start + tokens past the cache (or past max_keys) is not
+ * processed and leafq_device_status reports it. */
+int leafq_rotary_append_batch(void* stream, const float* qkv, int sequences, int64_t tokens, int heads,
+                              int kv_heads, int dim, int rotary_dim, const float* cos_table,
+                              const float* sin_table, const int32_t* positions, float* q_heads,
+                              float* k_cache, float* v_cache, int64_t capacity);
+/* Device workspace (bytes) leafq_attention_batch needs for this geometry,
+ * max_keys being a bound on positions[s] + tokens (0: none needed, the
+ * per-query form runs).  Prompts (16 or more tokens per sequence, head size
+ * 32 or 64) run a tiled form whose scores live in the workspace. */
+int64_t leafq_attention_workspace_bytes(int sequences, int64_t tokens, int heads, int kv_heads, int dim,
+                                        int64_t max_keys);
+int leafq_attention_batch(void* stream, const float* q_heads, const float* k_cache, const float* v_cache,
+                          int sequences, int64_t tokens, int heads, int kv_heads, int dim,
+                          const int32_t* positions, int64_t capacity, int64_t max_keys, float scale,
+                          float* out, void* workspace, int64_t workspace_bytes);
 /* gate_up [tokens][2 * width] with gate and up interleaved (g0, u0, g1, u1,
  * ..., the output of one linear over interleaved gate / up rows) -> out
  * [tokens][width] = u * (g / (1 + expf(-g))) (decoder.cpp:982-988, 1414). */
@@ -327,6 +349,8 @@ int leafq_argmax(void* stream, const float* logits, int64_t rows, int64_t width,
 int leafq_expf(void* stream, const float* x, int64_t n, float* y);
 /* *position += count on the stream. */
 int leafq_advance_position(void* stream, int32_t* position, int32_t count);
+/* positions[s] += count for every s < sequences, on the stream. */
+int leafq_advance_positions(void* stream, int32_t* positions, int sequences, int32_t count);
 
 #ifdef __cplusplus
 }

@@ -140,6 +140,11 @@ int leafq_device_status(void) {
     if (word == 0) return LEAFQ_OK;
     const unsigned int zero = 0;
     cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero));
+    if ((word >> 16) == kSiteCacheRange) {
+        set_error("a cache position was outside the KV cache (block " + std::to_string(word & 0xffffu) +
+                  "); the kernel skipped it");
+        return LEAFQ_ERR_INVALID;
+    }
     set_error("a device wait timed out (site " + std::to_string(word >> 16) + ", block " +
               std::to_string(word & 0xffffu) + ")");
     return LEAFQ_ERR_TIMEOUT;

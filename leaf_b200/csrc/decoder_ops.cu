@@ -135,32 +135,43 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(
 }
 
 // ------------------------------------------------------ rotary + KV append
-// qkv[t] = [q (heads*dim) | k (kv*dim) | v (kv*dim)].  Block (t, head):
-// heads first (q -> q_heads[head][t]), then kv heads (k -> k cache, v -> v cache).
+// Sequence s of a batch owns rows s*tokens .. s*tokens+tokens-1 of qkv, its
+// own cache [kv_heads][capacity][dim] at s * kv_heads * capacity * dim, and
+// its own start position positions[s].  qkv[row] = [q (heads*dim) | k
+// (kv*dim) | v (kv*dim)].  Block (t, head, s): heads first (q ->
+// q_heads[s][head][t]), then kv heads (k -> k cache, v -> v cache).  A
+// position past the cache is recorded in the device error word and skipped.
 __global__ void rotary_append_kernel(const float* __restrict__ qkv, int64_t tokens, int heads,
                                      int kv_heads, int dim, int rotary_dim,
                                      const float* __restrict__ cos_table,
                                      const float* __restrict__ sin_table,
-                                     const int32_t* __restrict__ position,
+                                     const int32_t* __restrict__ positions,
                                      float* __restrict__ q_heads, float* __restrict__ k_cache,
                                      float* __restrict__ v_cache, int64_t capacity) {
     const int64_t t = blockIdx.x;
     const int head = blockIdx.y;
+    const int64_t seq = blockIdx.z;
     const int64_t width = (int64_t)(heads + 2 * kv_heads) * dim;
-    const int64_t pos = static_cast<int64_t>(*position) + t;
+    const int64_t start = positions[seq];
+    const int64_t pos = start + t;
+    if (start < 0 || start + tokens > capacity) {
+        if (threadIdx.x == 0 && t == 0 && head == 0) record_device_error(kSiteCacheRange);
+        return;
+    }
     const int half = rotary_dim / 2;
-    const float* row = qkv + t * width;
+    const float* row = qkv + (seq * tokens + t) * width;
+    const int64_t cache = seq * kv_heads * capacity * dim;
     const float* src;
     float* dst;
     if (head < heads) {
         src = row + (int64_t)head * dim;
-        dst = q_heads + ((int64_t)head * tokens + t) * dim;
+        dst = q_heads + ((seq * heads + head) * tokens + t) * dim;
     } else {
         const int kvh = head - heads;
         src = row + (int64_t)heads * dim + (int64_t)kvh * dim;
-        dst = k_cache + ((int64_t)kvh * capacity + pos) * dim;
+        dst = k_cache + cache + ((int64_t)kvh * capacity + pos) * dim;
         const float* vsrc = row + (int64_t)(heads + kv_heads) * dim + (int64_t)kvh * dim;
-        float* vdst = v_cache + ((int64_t)kvh * capacity + pos) * dim;
+        float* vdst = v_cache + cache + ((int64_t)kvh * capacity + pos) * dim;
         for (int i = threadIdx.x; i < dim; i += blockDim.x) vdst[i] = vsrc[i];
     }
     for (int i = threadIdx.x; i < dim; i += blockDim.x) {
@@ -176,13 +187,22 @@ __global__ void rotary_append_kernel(const float* __restrict__ qkv, int64_t toke
 }
 
 // -------------------------------------------------------------- attention
-// Block (head, t): query t of this chunk attends keys [0, position + t]
-// (attention_impl, transformer.cpp:93-145).  out[t][head*dim + d].
+// Both kernels compute, for query t of sequence s and head h (kv head
+// kvh = h / (heads / kv_heads)), over keys 0 .. positions[s] + t
+// (attention_impl, transformer.cpp:93-145):
+//   score_k = (dot(q, k_k) * scale) * scale, the dot summed over d in order;
+//   e_k = expf(score_k - max_k score);  den = e_0 + e_1 + ... in key order;
+//   out[d] = sum over keys in order of (e_k / den) * v_k[d].
+// out[(s*tokens + t)][h*dim + d].
+//
+// attention_kernel: block (head, t, s), threads over keys for the dots, one
+// thread for the denominator, threads over d for the weighted sum; the form
+// for one or a few queries per sequence (decode).
 // Shared memory: q [dim], then scores [capacity].
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
     const float* __restrict__ q_heads, const float* __restrict__ k_cache,
     const float* __restrict__ v_cache, int64_t tokens, int heads, int kv_heads, int dim,
-    const int32_t* __restrict__ position, int64_t capacity, float scale, float* __restrict__ out,
+    const int32_t* __restrict__ positions, int64_t capacity, float scale, float* __restrict__ out,
     const __grid_constant__ ExpTable tab) {
     extern __shared__ float smem[];
     float* q = smem;
@@ -191,14 +211,20 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
     __shared__ float denominator_s;
     const int head = blockIdx.x;
     const int64_t t = blockIdx.y;
+    const int64_t seq = blockIdx.z;
     const int kvh = head / (heads / kv_heads);
-    const int64_t keys = static_cast<int64_t>(*position) + t + 1;
-    const float* qrow = q_heads + ((int64_t)head * tokens + t) * dim;
+    const int64_t start = positions[seq];
+    if (start < 0 || start + tokens > capacity) {
+        if (threadIdx.x == 0 && t == 0 && head == 0) record_device_error(kSiteCacheRange);
+        return;
+    }
+    const int64_t keys = start + t + 1;
+    const float* qrow = q_heads + ((seq * heads + head) * tokens + t) * dim;
     for (int i = threadIdx.x; i < dim; i += blockDim.x) q[i] = qrow[i];
     __syncthreads();
-    const float* kbase = k_cache + (int64_t)kvh * capacity * dim;
-    const float* vbase = v_cache + (int64_t)kvh * capacity * dim;
-    // scores[k] = dot(q, k) * scale * scale, the dot summed left to right.
+    const int64_t cache = seq * kv_heads * capacity * dim;
+    const float* kbase = k_cache + cache + (int64_t)kvh * capacity * dim;
+    const float* vbase = v_cache + cache + (int64_t)kvh * capacity * dim;
     float local_max = -INFINITY;
     for (int64_t k = threadIdx.x; k < keys; k += blockDim.x) {
         const float* krow = kbase + k * dim;
@@ -221,11 +247,139 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
     const float denominator = denominator_s;
     for (int64_t k = threadIdx.x; k < keys; k += blockDim.x) scores[k] = __fdiv_rn(scores[k], denominator);
     __syncthreads();
-    // out[d] = sum over keys, in order, of probability * value (thread per d).
     for (int d = threadIdx.x; d < dim; d += blockDim.x) {
         float acc = 0.0f;
         for (int64_t k = 0; k < keys; ++k) acc = __fadd_rn(acc, __fmul_rn(scores[k], vbase[k * dim + d]));
-        out[(t * heads + head) * (int64_t)dim + d] = acc;
+        out[((seq * tokens + t) * heads + head) * (int64_t)dim + d] = acc;
+    }
+}
+
+// attention_tile_kernel: the form for prompts (many queries per sequence).
+// One thread per (query, head) pair: a block takes kTileThreads / group
+// consecutive queries of one sequence and the `group` query heads of one kv
+// head, so every key and value row staged in shared memory serves all of
+// them.  Each thread keeps its query (DIM registers) for the dots and its
+// DIM output sums in registers, and runs its own denominator and output
+// sums in key order.  Scores, then exponentials, go to a per-block slice of
+// the global workspace, [max_keys][kTileThreads] (pair fastest: coalesced).
+// Blocks loop over (sequence, kv head, query tile) jobs.
+constexpr int kTileThreads = 128;
+constexpr int kTileKeys = 32;  // keys per staged chunk
+
+template <int DIM>
+__device__ __forceinline__ void stage_rows(float* __restrict__ dst, const float* __restrict__ src,
+                                           int rows) {
+    // rows x DIM floats, row-contiguous in both; float4 per thread.
+    const int n4 = rows * DIM / 4;
+    for (int i = threadIdx.x; i < n4; i += kTileThreads)
+        reinterpret_cast<float4*>(dst)[i] = __ldg(reinterpret_cast<const float4*>(src) + i);
+}
+
+template <int DIM>
+__global__ void __launch_bounds__(kTileThreads, 3) attention_tile_kernel(
+    const float* __restrict__ q_heads, const float* __restrict__ k_cache,
+    const float* __restrict__ v_cache, int sequences, int64_t tokens, int heads, int kv_heads,
+    const int32_t* __restrict__ positions, int64_t capacity, int64_t max_keys, float scale,
+    float* __restrict__ out, float* __restrict__ workspace, const __grid_constant__ ExpTable tab) {
+    __shared__ __align__(16) float rows_s[kTileKeys * DIM];
+    const int group = heads / kv_heads;
+    const int tq = kTileThreads / group;
+    const int pair_query = threadIdx.x / group, pair_head = threadIdx.x % group;
+    const int64_t tiles = (tokens + tq - 1) / tq;
+    const int64_t jobs = (int64_t)sequences * kv_heads * tiles;
+    float* mine = workspace + (int64_t)blockIdx.x * max_keys * kTileThreads + threadIdx.x;
+    for (int64_t job = blockIdx.x; job < jobs; job += gridDim.x) {
+        const int64_t tile = job % tiles;
+        const int kvh = static_cast<int>((job / tiles) % kv_heads);
+        const int64_t seq = job / tiles / kv_heads;
+        const int64_t start = positions[seq];
+        if (start < 0 || start + tokens > capacity || start + tokens > max_keys) {
+            if (threadIdx.x == 0) record_device_error(kSiteCacheRange);
+            continue;  // uniform across the block
+        }
+        const int64_t t = tile * tq + pair_query;
+        const bool live = t < tokens;
+        const int64_t block_keys = start + min64(tile * tq + tq, tokens);
+        const int64_t keys = live ? start + t + 1 : 0;
+        const int head = kvh * group + pair_head;
+        const int64_t cache = (seq * kv_heads + kvh) * capacity * DIM;
+
+        // Pass 1: scores to the workspace, and their maximum.
+        float q[DIM];
+        {
+            const float* qrow = q_heads + ((seq * heads + head) * tokens + (live ? t : 0)) * DIM;
+#pragma unroll
+            for (int d = 0; d < DIM; d += 4) {
+                const float4 v = __ldg(reinterpret_cast<const float4*>(qrow + d));
+                q[d] = v.x, q[d + 1] = v.y, q[d + 2] = v.z, q[d + 3] = v.w;
+            }
+        }
+        float maximum = -INFINITY;
+        for (int64_t c0 = 0; c0 < block_keys; c0 += kTileKeys) {
+            const int n = static_cast<int>(min64(kTileKeys, block_keys - c0));
+            __syncthreads();
+            stage_rows<DIM>(rows_s, k_cache + cache + c0 * DIM, n);
+            __syncthreads();
+            for (int kk = 0; kk < n; kk += 4) {
+                float dot[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+                for (int d = 0; d < DIM; d += 4) {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        // Rows past n hold stale values; their dots are dropped below.
+                        const float4 k = *reinterpret_cast<const float4*>(rows_s + (kk + j) * DIM + d);
+                        dot[j] = __fadd_rn(dot[j], __fmul_rn(q[d], k.x));
+                        dot[j] = __fadd_rn(dot[j], __fmul_rn(q[d + 1], k.y));
+                        dot[j] = __fadd_rn(dot[j], __fmul_rn(q[d + 2], k.z));
+                        dot[j] = __fadd_rn(dot[j], __fmul_rn(q[d + 3], k.w));
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int64_t key = c0 + kk + j;
+                    if (key < keys) {
+                        const float s = __fmul_rn(__fmul_rn(dot[j], scale), scale);
+                        mine[key * kTileThreads] = s;
+                        maximum = fmaxf(maximum, s);
+                    }
+                }
+            }
+        }
+        // Pass 2: exponentials and the denominator, in key order.
+        float den = 0.0f;
+        for (int64_t k = 0; k < keys; ++k) {
+            const float e = expf_libm(__fsub_rn(mine[k * kTileThreads], maximum), tab);
+            den = __fadd_rn(den, e);
+            mine[k * kTileThreads] = e;
+        }
+        // Pass 3: probability-weighted values, each output element in key order.
+        float acc[DIM];
+#pragma unroll
+        for (int d = 0; d < DIM; ++d) acc[d] = 0.0f;
+        for (int64_t c0 = 0; c0 < block_keys; c0 += kTileKeys) {
+            const int n = static_cast<int>(min64(kTileKeys, block_keys - c0));
+            __syncthreads();
+            stage_rows<DIM>(rows_s, v_cache + cache + c0 * DIM, n);
+            __syncthreads();
+            const int mine_n = static_cast<int>(max64(0, min64(n, keys - c0)));
+            for (int kk = 0; kk < mine_n; ++kk) {
+                const float p = __fdiv_rn(mine[(c0 + kk) * kTileThreads], den);
+#pragma unroll
+                for (int d = 0; d < DIM; d += 4) {
+                    const float4 v = *reinterpret_cast<const float4*>(rows_s + kk * DIM + d);
+                    acc[d] = __fadd_rn(acc[d], __fmul_rn(p, v.x));
+                    acc[d + 1] = __fadd_rn(acc[d + 1], __fmul_rn(p, v.y));
+                    acc[d + 2] = __fadd_rn(acc[d + 2], __fmul_rn(p, v.z));
+                    acc[d + 3] = __fadd_rn(acc[d + 3], __fmul_rn(p, v.w));
+                }
+            }
+        }
+        if (live) {
+            float* orow = out + ((seq * tokens + t) * heads + head) * (int64_t)DIM;
+#pragma unroll
+            for (int d = 0; d < DIM; d += 4)
+                *reinterpret_cast<float4*>(orow + d) = make_float4(acc[d], acc[d + 1], acc[d + 2], acc[d + 3]);
+        }
     }
 }
 
@@ -286,7 +440,9 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* __r
     }
 }
 
-__global__ void advance_kernel(int32_t* position, int32_t count) { *position += count; }
+__global__ void advance_kernel(int32_t* positions, int sequences, int32_t count) {
+    for (int i = threadIdx.x; i < sequences; i += blockDim.x) positions[i] += count;
+}
 
 __global__ void expf_kernel(const float* __restrict__ x, int64_t n, float* __restrict__ y,
                             const __grid_constant__ ExpTable tab) {
@@ -363,31 +519,112 @@ int leafq_rope_tables(float theta, int rotary_dim, int64_t positions, float* cos
     return LEAFQ_OK;
 }
 
-int leafq_rotary_append(void* stream, const float* qkv, int64_t tokens, int heads, int kv_heads,
-                        int dim, int rotary_dim, const float* cos_table, const float* sin_table,
-                        const int32_t* position, float* q_heads, float* k_cache, float* v_cache,
-                        int64_t capacity) {
+int leafq_rotary_append_batch(void* stream, const float* qkv, int sequences, int64_t tokens, int heads,
+                              int kv_heads, int dim, int rotary_dim, const float* cos_table,
+                              const float* sin_table, const int32_t* positions, float* q_heads,
+                              float* k_cache, float* v_cache, int64_t capacity) {
     clear_error();
-    if (tokens < 0 || heads <= 0 || kv_heads <= 0 || heads % kv_heads || dim <= 0 ||
-        rotary_dim < 0 || rotary_dim > dim || rotary_dim % 2 || capacity <= 0 || tokens > 65535) {
+    if (sequences < 0 || sequences > 65535 || tokens < 0 || heads <= 0 || kv_heads <= 0 ||
+        heads % kv_heads || dim <= 0 || rotary_dim < 0 || rotary_dim > dim || rotary_dim % 2 ||
+        capacity <= 0 || tokens > 65535) {
         set_error("leafq_rotary_append: invalid arguments");
         return LEAFQ_ERR_INVALID;
     }
-    if (tokens == 0) return LEAFQ_OK;
-    if (!qkv || !position || !q_heads || !k_cache || !v_cache || (rotary_dim && (!cos_table || !sin_table))) {
+    if (tokens == 0 || sequences == 0) return LEAFQ_OK;
+    if (!qkv || !positions || !q_heads || !k_cache || !v_cache || (rotary_dim && (!cos_table || !sin_table))) {
         set_error("leafq_rotary_append: null pointer");
         return LEAFQ_ERR_INVALID;
     }
     const int threads = dim < 128 ? ((dim + 31) / 32) * 32 : 128;
-    return launch(rotary_append_kernel, dim3(static_cast<unsigned>(tokens), heads + kv_heads),
+    return launch(rotary_append_kernel,
+                  dim3(static_cast<unsigned>(tokens), heads + kv_heads, static_cast<unsigned>(sequences)),
                   dim3(threads), 0, static_cast<cudaStream_t>(stream), false, "rotary_append", qkv,
-                  tokens, heads, kv_heads, dim, rotary_dim, cos_table, sin_table, position, q_heads,
+                  tokens, heads, kv_heads, dim, rotary_dim, cos_table, sin_table, positions, q_heads,
                   k_cache, v_cache, capacity);
+}
+
+int leafq_rotary_append(void* stream, const float* qkv, int64_t tokens, int heads, int kv_heads,
+                        int dim, int rotary_dim, const float* cos_table, const float* sin_table,
+                        const int32_t* position, float* q_heads, float* k_cache, float* v_cache,
+                        int64_t capacity) {
+    return leafq_rotary_append_batch(stream, qkv, 1, tokens, heads, kv_heads, dim, rotary_dim, cos_table,
+                                     sin_table, position, q_heads, k_cache, v_cache, capacity);
+}
+
+namespace {
+// The tile form serves prompts: enough queries per sequence to fill a
+// block's pairs, a head size it is compiled for, and 16-byte rows.
+bool attention_tile_form(int64_t tokens, int heads, int kv_heads, int dim) {
+    const int group = heads / kv_heads;
+    return (dim == 32 || dim == 64) && kTileThreads % group == 0 && tokens >= 16;
+}
+
+int64_t attention_tile_grid(int sequences, int64_t tokens, int heads, int kv_heads) {
+    const int tq = kTileThreads / (heads / kv_heads);
+    const int64_t jobs = (int64_t)sequences * kv_heads * ((tokens + tq - 1) / tq);
+    return std::min<int64_t>(jobs, static_cast<int64_t>(sm_count()) * 3);
+}
+}  // namespace
+
+int64_t leafq_attention_workspace_bytes(int sequences, int64_t tokens, int heads, int kv_heads, int dim,
+                                        int64_t max_keys) {
+    if (sequences <= 0 || tokens <= 0 || heads <= 0 || kv_heads <= 0 || heads % kv_heads || max_keys <= 0)
+        return 0;
+    if (!attention_tile_form(tokens, heads, kv_heads, dim)) return 0;
+    return attention_tile_grid(sequences, tokens, heads, kv_heads) * max_keys * kTileThreads *
+           static_cast<int64_t>(sizeof(float));
+}
+
+int leafq_attention_batch(void* stream, const float* q_heads, const float* k_cache, const float* v_cache,
+                          int sequences, int64_t tokens, int heads, int kv_heads, int dim,
+                          const int32_t* positions, int64_t capacity, int64_t max_keys, float scale,
+                          float* out, void* workspace, int64_t workspace_bytes) {
+    clear_error();
+    if (sequences < 0 || sequences > 65535 || tokens < 0 || heads <= 0 || kv_heads <= 0 ||
+        heads % kv_heads || dim <= 0 || dim > 1024 || capacity <= 0 || tokens > 65535 ||
+        !(scale > 0.0f) || max_keys < tokens || max_keys > capacity) {
+        set_error("leafq_attention: invalid arguments");
+        return LEAFQ_ERR_INVALID;
+    }
+    if (tokens == 0 || sequences == 0) return LEAFQ_OK;
+    if (!q_heads || !k_cache || !v_cache || !positions || !out) {
+        set_error("leafq_attention: null pointer");
+        return LEAFQ_ERR_INVALID;
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int64_t need = leafq_attention_workspace_bytes(sequences, tokens, heads, kv_heads, dim, max_keys);
+    if (need > 0 && aligned16(q_heads) && aligned16(k_cache) && aligned16(v_cache) && aligned16(out)) {
+        if (!workspace || workspace_bytes < need || !aligned16(workspace)) {
+            set_error("leafq_attention: workspace smaller than leafq_attention_workspace_bytes");
+            return LEAFQ_ERR_INVALID;
+        }
+        const int grid = static_cast<int>(attention_tile_grid(sequences, tokens, heads, kv_heads));
+        float* ws = static_cast<float*>(workspace);
+        if (dim == 32)
+            return launch(attention_tile_kernel<32>, dim3(grid), dim3(kTileThreads), 0, s, false, "attention",
+                          q_heads, k_cache, v_cache, sequences, tokens, heads, kv_heads, positions, capacity,
+                          max_keys, scale, out, ws, exp_table());
+        return launch(attention_tile_kernel<64>, dim3(grid), dim3(kTileThreads), 0, s, false, "attention",
+                      q_heads, k_cache, v_cache, sequences, tokens, heads, kv_heads, positions, capacity,
+                      max_keys, scale, out, ws, exp_table());
+    }
+    const size_t smem = (static_cast<size_t>(dim) + capacity) * sizeof(float);
+    if (smem > static_cast<size_t>(max_smem_per_block())) {
+        set_error("leafq_attention: context capacity exceeds shared memory");
+        return LEAFQ_ERR_UNSUPPORTED;
+    }
+    int st = allow_smem(reinterpret_cast<const void*>(attention_kernel), smem, "attention");
+    if (st) return st;
+    return launch(attention_kernel,
+                  dim3(heads, static_cast<unsigned>(tokens), static_cast<unsigned>(sequences)),
+                  dim3(kAttnThreads), smem, s, false, "attention", q_heads, k_cache, v_cache, tokens, heads,
+                  kv_heads, dim, positions, capacity, scale, out, exp_table());
 }
 
 int leafq_attention(void* stream, const float* q_heads, const float* k_cache, const float* v_cache,
                     int64_t tokens, int heads, int kv_heads, int dim, const int32_t* position,
                     int64_t capacity, float scale, float* out) {
+    // Without a workspace: the per-query form.
     clear_error();
     if (tokens < 0 || heads <= 0 || kv_heads <= 0 || heads % kv_heads || dim <= 0 || dim > 1024 ||
         capacity <= 0 || tokens > 65535 || !(scale > 0.0f)) {
@@ -406,9 +643,9 @@ int leafq_attention(void* stream, const float* q_heads, const float* k_cache, co
     }
     int st = allow_smem(reinterpret_cast<const void*>(attention_kernel), smem, "attention");
     if (st) return st;
-    return launch(attention_kernel, dim3(heads, static_cast<unsigned>(tokens)), dim3(kAttnThreads),
-                  smem, static_cast<cudaStream_t>(stream), false, "attention", q_heads, k_cache,
-                  v_cache, tokens, heads, kv_heads, dim, position, capacity, scale, out, exp_table());
+    return launch(attention_kernel, dim3(heads, static_cast<unsigned>(tokens), 1), dim3(kAttnThreads), smem,
+                  static_cast<cudaStream_t>(stream), false, "attention", q_heads, k_cache, v_cache, tokens,
+                  heads, kv_heads, dim, position, capacity, scale, out, exp_table());
 }
 
 int leafq_silu_gate(void* stream, const float* gate_up, int64_t tokens, int64_t width, float* out) {
@@ -456,14 +693,19 @@ int leafq_expf(void* stream, const float* x, int64_t n, float* y) {
                   static_cast<cudaStream_t>(stream), false, "expf", x, n, y, exp_table());
 }
 
-int leafq_advance_position(void* stream, int32_t* position, int32_t count) {
+int leafq_advance_positions(void* stream, int32_t* positions, int sequences, int32_t count) {
     clear_error();
-    if (!position || count < 0) {
+    if (!positions || count < 0 || sequences < 0) {
         set_error("leafq_advance_position: invalid arguments");
         return LEAFQ_ERR_INVALID;
     }
-    return launch(advance_kernel, dim3(1), dim3(1), 0, static_cast<cudaStream_t>(stream), false,
-                  "advance_position", position, count);
+    if (sequences == 0) return LEAFQ_OK;
+    return launch(advance_kernel, dim3(1), dim3(256), 0, static_cast<cudaStream_t>(stream), false,
+                  "advance_position", positions, sequences, count);
+}
+
+int leafq_advance_position(void* stream, int32_t* position, int32_t count) {
+    return leafq_advance_positions(stream, position, 1, count);
 }
 
 }  // extern "C"

@@ -45,6 +45,7 @@ enum WaitSite : unsigned {
     kSiteDecodeDependency = 11,
     kSiteDecodeCodes = 12,
     kSiteAllGather = 13,
+    kSiteCacheRange = 14,  // not a wait: a position outside the KV cache
 };
 
 __device__ __forceinline__ unsigned long long global_timer_ns() {
@@ -189,6 +190,7 @@ __device__ __forceinline__ bool elect_one_sync() {
 __device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
 
 __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
+__device__ __forceinline__ int64_t max64(int64_t a, int64_t b) { return a > b ? a : b; }
 
 // --------------------------------------------------------------- tcgen05
 __device__ __forceinline__ void tmem_alloc(uint32_t* smem_result, uint32_t ncols) {

@@ -67,10 +67,17 @@ def _concat_rows(parts: list[HostTensor], device: torch.device, interleave: bool
 
 class Decoder:
     def __init__(self, artifact, activation_bits: int = 8, device="cuda",
-                 capacity: Optional[int] = None):
+                 capacity: Optional[int] = None, sequences: int = 1):
         """artifact: a path, an ``Artifact``, or any object with the same
         ``config`` / ``get(name)`` interface whose payloads are tensors
-        (``leaf_b200.stack.random_decoder_model``)."""
+        (``leaf_b200.stack.RandomDecoderModel``).
+
+        sequences > 1 decodes that many independent requests together (one
+        KV cache and position per sequence, every linear over all of their
+        rows): ``forward_batch`` / ``generate_batch`` give each sequence the
+        tokens the single-sequence decoder gives it, bit for bit -- the
+        reference serves the same requests one after another
+        (main_decoder.cpp:233-300)."""
         art = artifact if hasattr(artifact, "get") else Artifact(artifact)
         cfg = art.config
         if not (cfg.norm_kind == 0 and cfg.position_kind == 0 and cfg.gated == 1 and
@@ -81,7 +88,10 @@ class Decoder:
                             "sliding window or Q/K norm")
         if activation_bits not in (8, 32):
             raise LeafError(_lib.LEAFQ_ERR_INVALID, "activation bits must be 8 or 32")
+        if sequences < 1:
+            raise LeafError(_lib.LEAFQ_ERR_INVALID, "sequences must be positive")
         self.cfg = cfg
+        self.sequences = int(sequences)
         self.activation_bits = activation_bits
         self.device = torch.device(device)
         self.capacity = int(capacity or cfg.max_positions)
@@ -118,7 +128,8 @@ class Decoder:
         self.final_norm = f32(art.get("model.norm.weight")) if cfg.final_norm else None
         self.lm_head = weight([art.get("lm_head.weight")])
         d, kv = cfg.head_dim, cfg.kv_heads
-        self.k_cache = [torch.zeros((kv, self.capacity, d), dtype=torch.float32, device=dev)
+        S = self.sequences
+        self.k_cache = [torch.zeros((S, kv, self.capacity, d), dtype=torch.float32, device=dev)
                         for _ in range(cfg.layers)]
         self.v_cache = [torch.zeros_like(k) for k in self.k_cache]
         half = cfg.rotary_dim // 2
@@ -130,12 +141,12 @@ class Decoder:
         self.sin = torch.from_numpy(sin).to(dev)
         # decoder.cpp:1348: both q and k are scaled by 1/sqrt(sqrt(dim)).
         self.scale = float(np.float32(1.0) / np.sqrt(np.sqrt(np.float32(d))))
-        self.position = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.position = torch.zeros(S, dtype=torch.int32, device=dev)
         self.error_flag = torch.zeros(1, dtype=torch.int32, device=dev)
         self.length = 0
         self._buffers: dict[int, dict] = {}
         self.graph: Optional[torch.cuda.CUDAGraph] = None
-        self.token = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.token = torch.zeros(S, dtype=torch.int32, device=dev)
         self.history = torch.zeros(self.capacity + 1, dtype=torch.int32, device=dev)
         self.step_logits = torch.zeros(cfg.vocab, dtype=torch.float32, device=dev)
         self._plan = None
@@ -143,25 +154,32 @@ class Decoder:
 
     # ------------------------------------------------------------ buffers
     def _bufs(self, tokens: int) -> dict:
+        """Buffers of one forward of `tokens` tokens per sequence."""
         b = self._buffers.get(tokens)
         if b is None:
             c = self.cfg
             q = c.heads * c.head_dim
             dev = self.device
+            S = self.sequences
+            rows = S * tokens
             e = lambda *s: torch.empty(s, dtype=torch.float32, device=dev)  # noqa: E731
-            b = dict(ids=torch.zeros(tokens, dtype=torch.int32, device=dev), hidden=e(tokens, c.hidden),
-                     normalized=e(tokens, c.hidden), qkv=e(tokens, q + 2 * c.kv_heads * c.head_dim),
-                     q_heads=e(c.heads, tokens, c.head_dim), attn=e(tokens, q), o=e(tokens, c.hidden),
-                     gate_up=e(tokens, 2 * c.intermediate), act=e(tokens, c.intermediate),
-                     down=e(tokens, c.hidden), logits=e(1, c.vocab), workspace=Workspace(dev))
+            b = dict(ids=torch.zeros(rows, dtype=torch.int32, device=dev), hidden=e(rows, c.hidden),
+                     normalized=e(rows, c.hidden), qkv=e(rows, q + 2 * c.kv_heads * c.head_dim),
+                     q_heads=e(S, c.heads, tokens, c.head_dim), attn=e(rows, q), o=e(rows, c.hidden),
+                     gate_up=e(rows, 2 * c.intermediate), act=e(rows, c.intermediate),
+                     down=e(rows, c.hidden), last=e(S, c.hidden), logits=e(S, c.vocab),
+                     workspace=Workspace(dev))
             # Each chunk size owns its workspace, sized once: a captured graph
             # keeps its pointers, so nothing it uses may be reallocated.
             for w in self._weights():
-                for rows in (tokens, 1):
-                    need = self.lib.leafq_linear_workspace_bytes(rows, w.cols, w.bits, w.group,
+                for r in (rows, S):
+                    need = self.lib.leafq_linear_workspace_bytes(r, w.cols, w.bits, w.group,
                                                                  self.activation_bits)
                     if need:
                         b["workspace"].get(need)
+            need = self.lib.leafq_attention_workspace_bytes(S, tokens, c.heads, c.kv_heads, c.head_dim,
+                                                            self.capacity)
+            b["attention_ws"] = torch.empty(max(need, 16), dtype=torch.uint8, device=dev)
             self._buffers[tokens] = b
         return b
 
@@ -185,47 +203,58 @@ class Decoder:
                                0))
 
     def _forward_device(self, b: dict, tokens: int) -> None:
-        """One forward of `tokens` ids already in b["ids"] at the device
-        position; logits of the last row in b["logits"]; position advanced."""
+        """One forward of `tokens` ids per sequence already in b["ids"] at
+        the device positions; logits of each sequence's last row in
+        b["logits"]; positions advanced."""
         c, lib, s = self.cfg, self.lib, _stream()
-        check(lib.leafq_embed(s, b["ids"].data_ptr(), tokens, self.embed_table.data_ptr(),
+        S = self.sequences
+        rows = S * tokens
+        check(lib.leafq_embed(s, b["ids"].data_ptr(), rows, self.embed_table.data_ptr(),
                               None if self.embed_scales is None else self.embed_scales.data_ptr(),
                               self.embed_bits, self.embed_group, c.vocab, c.hidden,
                               ctypes.c_float(c.embedding_scale), b["hidden"].data_ptr(),
                               self.error_flag.data_ptr()))
-        check(lib.leafq_rmsnorm(s, b["hidden"].data_ptr(), None, 0, tokens, c.hidden,
+        check(lib.leafq_rmsnorm(s, b["hidden"].data_ptr(), None, 0, rows, c.hidden,
                                 self.layers[0]["input_norm"].data_ptr(), ctypes.c_float(c.epsilon),
                                 b["normalized"].data_ptr()))
+        ws = b["attention_ws"]
         for i, layer in enumerate(self.layers):
-            self._linear(b["normalized"], layer["qkv"], b["qkv"], tokens, b["workspace"])
-            check(lib.leafq_rotary_append(s, b["qkv"].data_ptr(), tokens, c.heads, c.kv_heads,
-                                          c.head_dim, c.rotary_dim, self.cos.data_ptr(),
-                                          self.sin.data_ptr(), self.position.data_ptr(),
-                                          b["q_heads"].data_ptr(), self.k_cache[i].data_ptr(),
-                                          self.v_cache[i].data_ptr(), self.capacity))
-            check(lib.leafq_attention(s, b["q_heads"].data_ptr(), self.k_cache[i].data_ptr(),
-                                      self.v_cache[i].data_ptr(), tokens, c.heads, c.kv_heads,
-                                      c.head_dim, self.position.data_ptr(), self.capacity,
-                                      ctypes.c_float(self.scale), b["attn"].data_ptr()))
-            self._linear(b["attn"], layer["o"], b["o"], tokens, b["workspace"])
-            check(lib.leafq_rmsnorm(s, b["hidden"].data_ptr(), b["o"].data_ptr(), 0, tokens, c.hidden,
+            self._linear(b["normalized"], layer["qkv"], b["qkv"], rows, b["workspace"])
+            check(lib.leafq_rotary_append_batch(s, b["qkv"].data_ptr(), S, tokens, c.heads, c.kv_heads,
+                                                c.head_dim, c.rotary_dim, self.cos.data_ptr(),
+                                                self.sin.data_ptr(), self.position.data_ptr(),
+                                                b["q_heads"].data_ptr(), self.k_cache[i].data_ptr(),
+                                                self.v_cache[i].data_ptr(), self.capacity))
+            check(lib.leafq_attention_batch(s, b["q_heads"].data_ptr(), self.k_cache[i].data_ptr(),
+                                            self.v_cache[i].data_ptr(), S, tokens, c.heads, c.kv_heads,
+                                            c.head_dim, self.position.data_ptr(), self.capacity,
+                                            self.capacity, ctypes.c_float(self.scale), b["attn"].data_ptr(),
+                                            ws.data_ptr(), ws.numel()))
+            self._linear(b["attn"], layer["o"], b["o"], rows, b["workspace"])
+            check(lib.leafq_rmsnorm(s, b["hidden"].data_ptr(), b["o"].data_ptr(), 0, rows, c.hidden,
                                     layer["post_norm"].data_ptr(), ctypes.c_float(c.epsilon),
                                     b["normalized"].data_ptr()))
-            self._linear(b["normalized"], layer["gate_up"], b["gate_up"], tokens, b["workspace"])
-            check(lib.leafq_silu_gate(s, b["gate_up"].data_ptr(), tokens, c.intermediate,
+            self._linear(b["normalized"], layer["gate_up"], b["gate_up"], rows, b["workspace"])
+            check(lib.leafq_silu_gate(s, b["gate_up"].data_ptr(), rows, c.intermediate,
                                       b["act"].data_ptr()))
-            self._linear(b["act"], layer["down"], b["down"], tokens, b["workspace"])
+            self._linear(b["act"], layer["down"], b["down"], rows, b["workspace"])
             last = i + 1 == len(self.layers)
             norm = (self.layers[i + 1]["input_norm"] if not last else self.final_norm)
             if norm is not None:
-                check(lib.leafq_rmsnorm(s, b["hidden"].data_ptr(), b["down"].data_ptr(), 1, tokens,
+                check(lib.leafq_rmsnorm(s, b["hidden"].data_ptr(), b["down"].data_ptr(), 1, rows,
                                         c.hidden, norm.data_ptr(), ctypes.c_float(c.epsilon),
                                         b["normalized"].data_ptr()))
             else:  # no final norm: the logits read the residual stream itself
                 raise LeafError(_lib.LEAFQ_ERR_UNSUPPORTED, "artifacts without a final norm")
-        last_row = b["normalized"][tokens - 1:tokens]
-        self._linear(last_row, self.lm_head, b["logits"], 1, b["workspace"])
-        check(lib.leafq_advance_position(s, self.position.data_ptr(), tokens))
+        if tokens == 1:
+            last_rows = b["normalized"]
+        elif S == 1:
+            last_rows = b["normalized"][tokens - 1:tokens]
+        else:  # each sequence's last row, gathered into consecutive rows
+            b["last"].copy_(b["normalized"].view(S, tokens, c.hidden)[:, tokens - 1])
+            last_rows = b["last"]
+        self._linear(last_rows, self.lm_head, b["logits"], S, b["workspace"])
+        check(lib.leafq_advance_positions(s, self.position.data_ptr(), S, tokens))
 
     # ----------------------------------------------------------- public API
     def reset(self) -> None:
@@ -237,6 +266,8 @@ class Decoder:
         """Decoder::forward_into(ids, logits) with all_logits = false: the
         last position's logits [1, vocab] (a device tensor reused by later
         calls)."""
+        if self.sequences != 1:
+            raise LeafError(_lib.LEAFQ_ERR_INVALID, "a batched decoder runs forward_batch")
         ids = [int(i) for i in ids]
         if not ids:
             raise LeafError(_lib.LEAFQ_ERR_INVALID, "input tokens are empty")
@@ -259,7 +290,7 @@ class Decoder:
         saved = self.position.clone()
         with torch.cuda.stream(stream):
             self._forward_device(b, 1)  # warm-up outside capture (lazy loads, smem attributes)
-            check(self.lib.leafq_argmax(_stream(), b["logits"].data_ptr(), 1, self.cfg.vocab,
+            check(self.lib.leafq_argmax(_stream(), b["logits"].data_ptr(), self.sequences, self.cfg.vocab,
                                         b["ids"].data_ptr()))
         torch.cuda.current_stream(self.device).wait_stream(stream)
         torch.cuda.synchronize(self.device)
@@ -267,7 +298,7 @@ class Decoder:
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
             self._forward_device(b, 1)
-            check(self.lib.leafq_argmax(_stream(), b["logits"].data_ptr(), 1, self.cfg.vocab,
+            check(self.lib.leafq_argmax(_stream(), b["logits"].data_ptr(), self.sequences, self.cfg.vocab,
                                         b["ids"].data_ptr()))
         self.graph = graph
 
@@ -295,12 +326,65 @@ class Decoder:
             out[i:i + 1].copy_(step["ids"])
         return [int(t) for t in out[:produced].tolist()]
 
+    def forward_batch(self, prompts) -> torch.Tensor:
+        """forward() for every sequence of the batch at once: prompts is one
+        list of ids per sequence, all of the same length; returns each
+        sequence's last-position logits [sequences, vocab] (a device tensor
+        reused by later calls)."""
+        prompts = [[int(i) for i in p] for p in prompts]
+        if len(prompts) != self.sequences:
+            raise LeafError(_lib.LEAFQ_ERR_INVALID, "one prompt per sequence")
+        tokens = len(prompts[0])
+        if tokens == 0 or any(len(p) != tokens for p in prompts):
+            raise LeafError(_lib.LEAFQ_ERR_INVALID, "batched prompts must be non-empty and of equal length")
+        if self.length + tokens > min(self.cfg.max_positions, self.capacity):
+            raise LeafError(_lib.LEAFQ_ERR_INVALID, "context length exceeds artifact limit")
+        if any(i < 0 or i >= self.cfg.vocab for p in prompts for i in p):
+            raise LeafError(_lib.LEAFQ_ERR_INVALID, "token id exceeds vocabulary")
+        b = self._bufs(tokens)
+        b["ids"].copy_(torch.tensor(prompts, dtype=torch.int32).reshape(-1))
+        self._forward_device(b, tokens)
+        self.length += tokens
+        return b["logits"]
+
+    def generate_batch(self, prompts, max_new: int) -> list[list[int]]:
+        """generate() for every sequence of the batch: one prefill over all
+        prompts, then one graph replay per token for all sequences.  A
+        sequence that reaches an EOS id stops there (its later tokens are
+        computed with the batch and dropped), as the reference's loop does."""
+        if max_new < 1:
+            raise LeafError(_lib.LEAFQ_ERR_INVALID, "max_new must be positive")
+        if self.graph is None:
+            self.capture_decode()
+        tokens = len(prompts[0]) if prompts else 0
+        if self.length + tokens + max_new - 1 > min(self.cfg.max_positions, self.capacity):
+            raise LeafError(_lib.LEAFQ_ERR_INVALID, "context length exceeds artifact limit")
+        logits = self.forward_batch(prompts)
+        step = self._bufs(1)
+        check(self.lib.leafq_argmax(_stream(), logits.data_ptr(), self.sequences, self.cfg.vocab,
+                                    step["ids"].data_ptr()))
+        out = torch.empty((max_new, self.sequences), dtype=torch.int32, device=self.device)
+        out[0].copy_(step["ids"])
+        for i in range(1, max_new):
+            self.graph.replay()
+            out[i].copy_(step["ids"])
+        self.length += max_new - 1
+        eos = set(self.cfg.eos_tokens)
+        result = []
+        for seq in out.t().tolist():
+            for i, t in enumerate(seq):
+                if t in eos:
+                    seq = seq[:i + 1]
+                    break
+            result.append(seq)
+        return result
+
     # ------------------------------------------------ whole-step kernel
     def fused_supported(self) -> bool:
         """The one-launch decode step needs per-row INT8 weights and
         embedding, W8A8, and a cache of at most 4096 rows."""
         per_row = all(w.bits == 8 and w.group == w.cols for w in self._weights())
-        return (per_row and self.activation_bits == 8 and self.embed_bits == 8 and
+        return (per_row and self.sequences == 1 and self.activation_bits == 8 and self.embed_bits == 8 and
                 self.embed_group == self.cfg.hidden and self.capacity <= 4096 and
                 self.final_norm is not None)
 
