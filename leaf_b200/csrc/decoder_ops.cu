@@ -138,9 +138,10 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(
 // Sequence s of a batch owns rows s*tokens .. s*tokens+tokens-1 of qkv, its
 // own cache [kv_heads][capacity][dim] at s * kv_heads * capacity * dim, and
 // its own start position positions[s].  qkv[row] = [q (heads*dim) | k
-// (kv*dim) | v (kv*dim)].  Block (t, head, s): heads first (q ->
-// q_heads[s][head][t]), then kv heads (k -> k cache, v -> v cache).  A
-// position past the cache is recorded in the device error word and skipped.
+// (kv*dim) | v (kv*dim)].  Block (t, s) rotates every q head (to
+// q_heads[s][head][t]) and k head (to the k cache) of its row and copies v
+// to the v cache.  A position past the cache is recorded in the device
+// error word and skipped.
 __global__ void rotary_append_kernel(const float* __restrict__ qkv, int64_t tokens, int heads,
                                      int kv_heads, int dim, int rotary_dim,
                                      const float* __restrict__ cos_table,
@@ -149,40 +150,40 @@ __global__ void rotary_append_kernel(const float* __restrict__ qkv, int64_t toke
                                      float* __restrict__ q_heads, float* __restrict__ k_cache,
                                      float* __restrict__ v_cache, int64_t capacity) {
     const int64_t t = blockIdx.x;
-    const int head = blockIdx.y;
-    const int64_t seq = blockIdx.z;
+    const int64_t seq = blockIdx.y;
     const int64_t width = (int64_t)(heads + 2 * kv_heads) * dim;
     const int64_t start = positions[seq];
     const int64_t pos = start + t;
     if (start < 0 || start + tokens > capacity) {
-        if (threadIdx.x == 0 && t == 0 && head == 0) record_device_error(kSiteCacheRange);
+        if (threadIdx.x == 0 && t == 0) record_device_error(kSiteCacheRange);
         return;
     }
     const int half = rotary_dim / 2;
     const float* row = qkv + (seq * tokens + t) * width;
     const int64_t cache = seq * kv_heads * capacity * dim;
-    const float* src;
-    float* dst;
-    if (head < heads) {
-        src = row + (int64_t)head * dim;
-        dst = q_heads + ((seq * heads + head) * tokens + t) * dim;
-    } else {
-        const int kvh = head - heads;
-        src = row + (int64_t)heads * dim + (int64_t)kvh * dim;
-        dst = k_cache + cache + ((int64_t)kvh * capacity + pos) * dim;
-        const float* vsrc = row + (int64_t)(heads + kv_heads) * dim + (int64_t)kvh * dim;
-        float* vdst = v_cache + cache + ((int64_t)kvh * capacity + pos) * dim;
-        for (int i = threadIdx.x; i < dim; i += blockDim.x) vdst[i] = vsrc[i];
-    }
-    for (int i = threadIdx.x; i < dim; i += blockDim.x) {
+    const float* cs = cos_table + pos * half;
+    const float* sn = sin_table + pos * half;
+    // Rotated heads: q heads 0..heads-1, then k heads.
+    const int rotated = heads + kv_heads;
+    for (int idx = threadIdx.x; idx < rotated * dim; idx += blockDim.x) {
+        const int head = idx / dim, i = idx - head * dim;
+        if (i >= half && i < rotary_dim) continue;  // written with its pair
+        const float* src = row + (int64_t)head * dim;
+        float* dst = head < heads ? q_heads + ((seq * heads + head) * tokens + t) * dim
+                                  : k_cache + cache + ((int64_t)(head - heads) * capacity + pos) * dim;
         if (i < half) {
-            const float c = cos_table[pos * half + i], s = sin_table[pos * half + i];
+            const float c = cs[i], sv = sn[i];
             const float a = src[i], b = src[i + half];
-            dst[i] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
-            dst[i + half] = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
-        } else if (i >= rotary_dim) {
+            dst[i] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, sv));
+            dst[i + half] = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, sv));
+        } else {
             dst[i] = src[i];
         }
+    }
+    const float* vsrc = row + (int64_t)rotated * dim;
+    for (int idx = threadIdx.x; idx < kv_heads * dim; idx += blockDim.x) {
+        const int kvh = idx / dim, i = idx - kvh * dim;
+        v_cache[cache + ((int64_t)kvh * capacity + pos) * dim + i] = vsrc[idx];
     }
 }
 
@@ -251,6 +252,164 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
         float acc = 0.0f;
         for (int64_t k = 0; k < keys; ++k) acc = __fadd_rn(acc, __fmul_rn(scores[k], vbase[k * dim + d]));
         out[((seq * tokens + t) * heads + head) * (int64_t)dim + d] = acc;
+    }
+}
+
+// attention_group_kernel: the decode form.  Block (t, kv head, s) serves
+// the `group` query heads that share one kv head, so each key and value row
+// is staged in shared memory once for all of them (coalesced loads; the next
+// chunk is loaded into registers while the current one is used).
+//   dots:  thread (h, k) of a chunk of min(64, kGroupThreads / group) keys,
+//          its dot over d in order (rows padded to DIM + 1 floats: no bank
+//          conflicts);
+//   softmax: exponentials by all threads, one thread per head for the
+//          denominator in key order, division by all threads;
+//   values: thread (h, d), its sum over keys in order.
+// Dynamic shared memory: scores [group][ld], ld = capacity rounded up to 4.
+constexpr int kGroupThreads = 256;
+constexpr int kGroupMaxHeads = 8;  // query heads per kv head served by this form
+constexpr int kGroupRows = 64;     // rows per staged chunk, at most
+
+template <int DIM>
+__device__ __forceinline__ void fetch_rows(float4 (&buf)[(kGroupRows * DIM / 4 + kGroupThreads - 1) / kGroupThreads],
+                                           const float* __restrict__ base, int n) {
+    constexpr int kF4 = (kGroupRows * DIM / 4 + kGroupThreads - 1) / kGroupThreads;
+#pragma unroll
+    for (int j = 0; j < kF4; ++j) {
+        const int i = threadIdx.x + j * kGroupThreads;
+        if (i < n * (DIM / 4)) buf[j] = __ldg(reinterpret_cast<const float4*>(base) + i);
+    }
+}
+
+template <int DIM>
+__global__ void __launch_bounds__(kGroupThreads) attention_group_kernel(
+    const float* __restrict__ q_heads, const float* __restrict__ k_cache,
+    const float* __restrict__ v_cache, int64_t tokens, int heads, int kv_heads,
+    const int32_t* __restrict__ positions, int64_t capacity, float scale, float* __restrict__ out,
+    const __grid_constant__ ExpTable tab) {
+    constexpr int kRowF4 = DIM / 4;
+    constexpr int kF4 = (kGroupRows * kRowF4 + kGroupThreads - 1) / kGroupThreads;
+    extern __shared__ __align__(16) float scores[];
+    __shared__ float q_s[kGroupMaxHeads * DIM];
+    __shared__ __align__(16) float rows_s[kGroupRows * (DIM + 1)];
+    __shared__ float red[kGroupThreads / 32];
+    __shared__ float max_s[kGroupMaxHeads], den_s[kGroupMaxHeads];
+    const int group = heads / kv_heads;
+    const int chunk = min(kGroupRows, kGroupThreads / group);  // 32 or 64 keys
+    const int64_t t = blockIdx.x;
+    const int kvh = blockIdx.y;
+    const int64_t seq = blockIdx.z;
+    const int64_t start = positions[seq];
+    if (start < 0 || start + tokens > capacity) {
+        if (threadIdx.x == 0 && t == 0 && kvh == 0) record_device_error(kSiteCacheRange);
+        return;
+    }
+    const int64_t keys = start + t + 1;
+    const int64_t ld = (capacity + 3) & ~static_cast<int64_t>(3);
+    const int64_t cache = (seq * kv_heads + kvh) * capacity * DIM;
+    const float* kbase = k_cache + cache;
+    const float* vbase = v_cache + cache;
+    const int tid = threadIdx.x;
+    for (int i = tid; i < group * DIM; i += kGroupThreads) {
+        const int h = i / DIM, d = i % DIM;
+        q_s[i] = q_heads[((seq * heads + kvh * group + h) * tokens + t) * DIM + d];
+    }
+    // ---- dots
+    const int my_h = tid / chunk, my_k = tid % chunk;
+    const bool dotter = my_h < group;
+    float4 pre[kF4];
+    fetch_rows<DIM>(pre, kbase, static_cast<int>(min64(chunk, keys)));
+    float local_max = -INFINITY;
+    for (int64_t c0 = 0; c0 < keys; c0 += chunk) {
+        const int n = static_cast<int>(min64(chunk, keys - c0));
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < kF4; ++j) {
+            const int i = tid + j * kGroupThreads;
+            if (i < n * kRowF4) {
+                float* dst = rows_s + (i / kRowF4) * (DIM + 1) + (i % kRowF4) * 4;
+                dst[0] = pre[j].x, dst[1] = pre[j].y, dst[2] = pre[j].z, dst[3] = pre[j].w;
+            }
+        }
+        __syncthreads();
+        if (c0 + chunk < keys)
+            fetch_rows<DIM>(pre, kbase + (c0 + chunk) * DIM, static_cast<int>(min64(chunk, keys - c0 - chunk)));
+        if (dotter && my_k < n) {
+            const float* kr = rows_s + my_k * (DIM + 1);
+            const float* qh = q_s + my_h * DIM;
+            float dot = 0.0f;
+#pragma unroll
+            for (int d = 0; d < DIM; ++d) dot = __fadd_rn(dot, __fmul_rn(qh[d], kr[d]));
+            const float sc = __fmul_rn(__fmul_rn(dot, scale), scale);
+            scores[my_h * ld + c0 + my_k] = sc;
+            local_max = fmaxf(local_max, sc);
+        }
+    }
+    // ---- per-head maximum (each warp lies within one head: chunk >= 32)
+    for (int o = 16; o > 0; o >>= 1) local_max = fmaxf(local_max, __shfl_xor_sync(0xffffffffu, local_max, o));
+    if ((tid & 31) == 0) red[tid >> 5] = local_max;
+    // Start the first value chunk while the softmax runs.
+    fetch_rows<DIM>(pre, vbase, static_cast<int>(min64(kGroupRows, keys)));
+    __syncthreads();
+    if (tid < group) {
+        const int warps_per_head = chunk / 32;
+        float m = -INFINITY;
+        for (int w = 0; w < warps_per_head; ++w) m = fmaxf(m, red[tid * warps_per_head + w]);
+        max_s[tid] = m;
+    }
+    __syncthreads();
+    for (int i = tid; i < group * chunk; i += kGroupThreads) {
+        const int h = i / chunk;
+        const float m = max_s[h];
+        for (int64_t k = i % chunk; k < keys; k += chunk)
+            scores[h * ld + k] = expf_libm(__fsub_rn(scores[h * ld + k], m), tab);
+    }
+    __syncthreads();
+    if (tid < group) {
+        const float* row = scores + tid * ld;
+        const int64_t body = keys & ~static_cast<int64_t>(3);
+        float den = sum_in_order(row, static_cast<int>(body));
+        for (int64_t k = body; k < keys; ++k) den = __fadd_rn(den, row[k]);
+        den_s[tid] = den;
+    }
+    __syncthreads();
+    for (int i = tid; i < group * chunk; i += kGroupThreads) {
+        const int h = i / chunk;
+        const float den = den_s[h];
+        for (int64_t k = i % chunk; k < keys; k += chunk) scores[h * ld + k] = __fdiv_rn(scores[h * ld + k], den);
+    }
+    // ---- probability-weighted values: thread (h, d) for h = h0, h0 + kPass, ...
+    constexpr int kPass = kGroupThreads / DIM;  // heads per pass of the block
+    constexpr int kAcc = (kGroupMaxHeads + kPass - 1) / kPass;
+    const int d = tid % DIM, h0 = tid / DIM;
+    float acc[kAcc];
+#pragma unroll
+    for (int j = 0; j < kAcc; ++j) acc[j] = 0.0f;
+    for (int64_t c0 = 0; c0 < keys; c0 += kGroupRows) {
+        const int n = static_cast<int>(min64(kGroupRows, keys - c0));
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < kF4; ++j) {
+            const int i = tid + j * kGroupThreads;
+            if (i < n * kRowF4) reinterpret_cast<float4*>(rows_s)[i] = pre[j];
+        }
+        __syncthreads();
+        if (c0 + kGroupRows < keys)
+            fetch_rows<DIM>(pre, vbase + (c0 + kGroupRows) * DIM,
+                            static_cast<int>(min64(kGroupRows, keys - c0 - kGroupRows)));
+        for (int k = 0; k < n; ++k) {
+            const float v = rows_s[k * DIM + d];
+#pragma unroll
+            for (int j = 0; j < kAcc; ++j) {
+                const int h = h0 + j * kPass;
+                if (h < group) acc[j] = __fadd_rn(acc[j], __fmul_rn(scores[h * ld + c0 + k], v));
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < kAcc; ++j) {
+        const int h = h0 + j * kPass;
+        if (h < group) out[((seq * tokens + t) * heads + kvh * group + h) * (int64_t)DIM + d] = acc[j];
     }
 }
 
@@ -345,12 +504,28 @@ __global__ void __launch_bounds__(kTileThreads, 3) attention_tile_kernel(
                 }
             }
         }
-        // Pass 2: exponentials and the denominator, in key order.
+        // Pass 2: exponentials and the denominator, in key order; the scores
+        // of the next 16 keys are loaded while the current 16 are used.
         float den = 0.0f;
-        for (int64_t k = 0; k < keys; ++k) {
-            const float e = expf_libm(__fsub_rn(mine[k * kTileThreads], maximum), tab);
-            den = __fadd_rn(den, e);
-            mine[k * kTileThreads] = e;
+        {
+            constexpr int kB = 16;
+            float cur[kB], nxt[kB];
+#pragma unroll
+            for (int j = 0; j < kB; ++j) cur[j] = j < keys ? mine[j * kTileThreads] : 0.0f;
+            for (int64_t k0 = 0; k0 < keys; k0 += kB) {
+#pragma unroll
+                for (int j = 0; j < kB; ++j) nxt[j] = k0 + kB + j < keys ? mine[(k0 + kB + j) * kTileThreads] : 0.0f;
+#pragma unroll
+                for (int j = 0; j < kB; ++j) {
+                    if (k0 + j < keys) {
+                        const float e = expf_libm(__fsub_rn(cur[j], maximum), tab);
+                        den = __fadd_rn(den, e);
+                        mine[(k0 + j) * kTileThreads] = e;
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < kB; ++j) cur[j] = nxt[j];
+            }
         }
         // Pass 3: probability-weighted values, each output element in key order.
         float acc[DIM];
@@ -362,8 +537,11 @@ __global__ void __launch_bounds__(kTileThreads, 3) attention_tile_kernel(
             stage_rows<DIM>(rows_s, v_cache + cache + c0 * DIM, n);
             __syncthreads();
             const int mine_n = static_cast<int>(max64(0, min64(n, keys - c0)));
+            float e_next = mine_n > 0 ? mine[c0 * kTileThreads] : 0.0f;
             for (int kk = 0; kk < mine_n; ++kk) {
-                const float p = __fdiv_rn(mine[(c0 + kk) * kTileThreads], den);
+                const float e = e_next;
+                if (kk + 1 < mine_n) e_next = mine[(c0 + kk + 1) * kTileThreads];
+                const float p = __fdiv_rn(e, den);
 #pragma unroll
                 for (int d = 0; d < DIM; d += 4) {
                     const float4 v = *reinterpret_cast<const float4*>(rows_s + kk * DIM + d);
@@ -386,15 +564,31 @@ __global__ void __launch_bounds__(kTileThreads, 3) attention_tile_kernel(
 // -------------------------------------------------------------- silu gate
 // gate_up[t] = [g0, u0, g1, u1, ...] (gate and up rows interleaved);
 // out[t][j] = u_j * (g_j / (1 + expf(-g_j))).
+__device__ __forceinline__ float silu_gate_one(float g, float u, const ExpTable& tab) {
+    return __fmul_rn(u, __fdiv_rn(g, __fadd_rn(1.0f, expf_libm(-g, tab))));
+}
+
+// Outputs are consecutive in memory (out [tokens][width] row-major and
+// gate_up its interleaved pairs), so the flat index i covers every token.
 __global__ void silu_gate_kernel(const float* __restrict__ gate_up, int64_t tokens, int64_t width,
-                                 float* __restrict__ out, const __grid_constant__ ExpTable tab) {
+                                 float* __restrict__ out, int vec, const __grid_constant__ ExpTable tab) {
     const int64_t n = tokens * width;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t t = i / width, j = i - t * width;
-        const float2 gu = reinterpret_cast<const float2*>(gate_up)[t * width + j];
-        const float g = gu.x, u = gu.y;
-        out[i] = __fmul_rn(u, __fdiv_rn(g, __fadd_rn(1.0f, expf_libm(-g, tab))));
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t first = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (vec) {
+        // Four outputs per thread and step: two float4 loads, one float4 store.
+        const float4* gu4 = reinterpret_cast<const float4*>(gate_up);
+        float4* o4 = reinterpret_cast<float4*>(out);
+        for (int64_t i = first; i < n / 4; i += stride) {
+            const float4 a = __ldg(gu4 + 2 * i), b = __ldg(gu4 + 2 * i + 1);
+            o4[i] = make_float4(silu_gate_one(a.x, a.y, tab), silu_gate_one(a.z, a.w, tab),
+                                silu_gate_one(b.x, b.y, tab), silu_gate_one(b.z, b.w, tab));
+        }
+        return;
+    }
+    for (int64_t i = first; i < n; i += stride) {
+        const float2 gu = reinterpret_cast<const float2*>(gate_up)[i];
+        out[i] = silu_gate_one(gu.x, gu.y, tab);
     }
 }
 
@@ -535,10 +729,8 @@ int leafq_rotary_append_batch(void* stream, const float* qkv, int sequences, int
         set_error("leafq_rotary_append: null pointer");
         return LEAFQ_ERR_INVALID;
     }
-    const int threads = dim < 128 ? ((dim + 31) / 32) * 32 : 128;
-    return launch(rotary_append_kernel,
-                  dim3(static_cast<unsigned>(tokens), heads + kv_heads, static_cast<unsigned>(sequences)),
-                  dim3(threads), 0, static_cast<cudaStream_t>(stream), false, "rotary_append", qkv,
+    return launch(rotary_append_kernel, dim3(static_cast<unsigned>(tokens), static_cast<unsigned>(sequences)),
+                  dim3(256), 0, static_cast<cudaStream_t>(stream), false, "rotary_append", qkv,
                   tokens, heads, kv_heads, dim, rotary_dim, cos_table, sin_table, positions, q_heads,
                   k_cache, v_cache, capacity);
 }
@@ -608,6 +800,25 @@ int leafq_attention_batch(void* stream, const float* q_heads, const float* k_cac
                       q_heads, k_cache, v_cache, sequences, tokens, heads, kv_heads, positions, capacity,
                       max_keys, scale, out, ws, exp_table());
     }
+    const int group = heads / kv_heads;
+    const int64_t ld = (capacity + 3) & ~static_cast<int64_t>(3);
+    const size_t group_smem = static_cast<size_t>(group) * ld * sizeof(float);
+    if ((dim == 32 || dim == 64) && group <= kGroupMaxHeads && aligned16(k_cache) && aligned16(v_cache) &&
+        group_smem + 24 * 1024 <= static_cast<size_t>(max_smem_per_block())) {
+        const dim3 grid(static_cast<unsigned>(tokens), kv_heads, static_cast<unsigned>(sequences));
+        if (dim == 32) {
+            int st = allow_smem(reinterpret_cast<const void*>(attention_group_kernel<32>), group_smem, "attention");
+            if (st) return st;
+            return launch(attention_group_kernel<32>, grid, dim3(kGroupThreads), group_smem, s, false,
+                          "attention", q_heads, k_cache, v_cache, tokens, heads, kv_heads, positions, capacity,
+                          scale, out, exp_table());
+        }
+        int st = allow_smem(reinterpret_cast<const void*>(attention_group_kernel<64>), group_smem, "attention");
+        if (st) return st;
+        return launch(attention_group_kernel<64>, grid, dim3(kGroupThreads), group_smem, s, false, "attention",
+                      q_heads, k_cache, v_cache, tokens, heads, kv_heads, positions, capacity, scale, out,
+                      exp_table());
+    }
     const size_t smem = (static_cast<size_t>(dim) + capacity) * sizeof(float);
     if (smem > static_cast<size_t>(max_smem_per_block())) {
         set_error("leafq_attention: context capacity exceeds shared memory");
@@ -660,9 +871,11 @@ int leafq_silu_gate(void* stream, const float* gate_up, int64_t tokens, int64_t 
         return LEAFQ_ERR_INVALID;
     }
     const int64_t n = tokens * width;
-    const int64_t blocks = std::min<int64_t>((n + 255) / 256, static_cast<int64_t>(sm_count()) * 8);
+    const int vec = (n % 4 == 0) && aligned16(gate_up) && aligned16(out);
+    const int64_t items = vec ? n / 4 : n;
+    const int64_t blocks = std::min<int64_t>((items + 255) / 256, static_cast<int64_t>(sm_count()) * 8);
     return launch(silu_gate_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0,
-                  static_cast<cudaStream_t>(stream), false, "silu_gate", gate_up, tokens, width, out,
+                  static_cast<cudaStream_t>(stream), false, "silu_gate", gate_up, tokens, width, out, vec,
                   exp_table());
 }
 

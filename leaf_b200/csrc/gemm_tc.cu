@@ -9,9 +9,10 @@
 //   y = fma(float(acc) * sx[token], sw[row], 0.0f) + (bias[row] or 0.0f).
 //
 // Tiling: D[128 tokens, BN rows] per tile (one UMMA of M=128, N=BN, K=32
-// per instruction, four per 128-byte K block); BN = 256, or 128 when the
-// 256-wide tiles would leave SMs idle (few tokens: prefill chunks of a few
-// hundred tokens), so that every SM gets a tile.  Operands are K-major: the
+// per instruction, four per 128-byte K block); BN = 256, or the widest of
+// 128 / 64 / 32 whose tiles still give every SM one (few tokens: prefill
+// chunks, batched decode of a few dozen sequences, where the weight stream
+// is the cost and must come through all SMs), else 32.  Operands are K-major: the
 // codes [tokens, cols] and the weights [rows, cols] are both row-major with
 // K contiguous, loaded by TMA with 128-byte swizzle into a 4-stage ring
 // (48 KB per stage).  Warp roles (192 threads, persistent over tiles):
@@ -40,7 +41,8 @@ constexpr int kABytes = BM * BK;  // 16 KB
 
 template <int BN>
 struct TileCfg {
-    static constexpr int kStages = BN == 256 ? 4 : 6;
+    // As many 128-byte K stages as fit in ~200 KB of shared memory.
+    static constexpr int kStages = BN == 256 ? 4 : BN == 128 ? 6 : BN == 64 ? 8 : 10;
     static constexpr int kAccCols = BN;  // TMEM columns per accumulator
     static constexpr int kTmemCols = 2 * kAccCols;
     static constexpr int kBBytes = BN * BK;
@@ -303,9 +305,11 @@ int launch_gemm_tc(cudaStream_t s, const int8_t* q, const float* sx, int64_t tok
     a.rows = rows;
     a.cols = cols;
     a.m_tiles = static_cast<int>((tokens + BM - 1) / BM);
-    const int64_t wide_tiles = (int64_t)a.m_tiles * ((rows + 255) / 256);
-    if (wide_tiles >= sm_count()) return run_tiles<256>(s, q, weight, cols, tokens, rows, a, pdl);
-    return run_tiles<128>(s, q, weight, cols, tokens, rows, a, pdl);
+    auto tiles = [&](int64_t bn) { return (int64_t)a.m_tiles * ((rows + bn - 1) / bn); };
+    if (tiles(256) >= sm_count()) return run_tiles<256>(s, q, weight, cols, tokens, rows, a, pdl);
+    if (tiles(128) >= sm_count()) return run_tiles<128>(s, q, weight, cols, tokens, rows, a, pdl);
+    if (tiles(64) >= sm_count()) return run_tiles<64>(s, q, weight, cols, tokens, rows, a, pdl);
+    return run_tiles<32>(s, q, weight, cols, tokens, rows, a, pdl);
 }
 
 }  // namespace leafq
