@@ -49,6 +49,13 @@ def parse():
     p.add_argument("--cpu-tokens", type=int, default=32,
                    help="tokens the bounded CPU-baseline sample generates (rank 0, N=1)")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--workload", choices=("decode", "batch"), default="decode",
+                   help="decode: config 3 (batch 1, the headline); batch: config 4 (64 sequences x "
+                        "512-token prompts, 256 greedy tokens each, split over the ranks)")
+    p.add_argument("--batch-split", choices=("dp", "tp"), default="dp",
+                   help="batch workload on N GPUs: dp = the sequences split over the ranks (full "
+                        "weights each); tp = every linear's rows split over the ranks with an NCCL "
+                        "all-gather of each output (all sequences on every rank)")
     p.add_argument("--case", choices=sorted(CASES),
                    help="run one small single-kernel case three times and exit (for ncu captures)")
     return p.parse_args()
@@ -166,7 +173,7 @@ def workload_config(n_gpus):
 
 
 # ----------------------------------------------------------------- CPU side
-def cpu_reference_decoder(threads: int, new_tokens: int, warmup: int = 0):
+def cpu_reference_decoder(threads: int, new_tokens: int, warmup: int = 0, prompt: int = PROMPT):
     """The reference's own CPU decoder (oracle/_ref/leaf_decoder built from
     engine/src/decoder.cpp with leaf/cli.py's flags) on a TinyLlama-shaped
     W8A8 artifact (seeded random weights written by oracle/fixture.py in the
@@ -183,7 +190,7 @@ def cpu_reference_decoder(threads: int, new_tokens: int, warmup: int = 0):
         work = Path(tmp)
         art = work / "tinyllama_w8.leaf"
         fx.write_artifact(art, fx.TINYLLAMA, fx.llama_tensors(fx.TINYLLAMA, 7, 0.0), 8, 64)
-        ids = fx.prompt_ids(fx.TINYLLAMA, 3, PROMPT)
+        ids = fx.prompt_ids(fx.TINYLLAMA, 3, prompt)
         with (work / "tokens.bin").open("wb") as f:
             f.write(np.asarray([1, len(ids)], dtype="<u4").tobytes())
             f.write(np.asarray(ids, dtype="<u4").tobytes())
@@ -196,7 +203,7 @@ def cpu_reference_decoder(threads: int, new_tokens: int, warmup: int = 0):
     if not steps:
         raise RuntimeError("reference decoder reported no decode steps")
     per_ms = float(np.mean(steps))
-    sample = (f"{len(steps)} greedy decode steps (positions {PROMPT}..{PROMPT + len(steps) - 1}) of the "
+    sample = (f"{len(steps)} greedy decode steps (positions {prompt}..{prompt + len(steps) - 1}) of the "
               f"reference decoder bench-generate on a TinyLlama-shape W8A8 artifact, {threads} threads")
     return 1000.0 / per_ms, sample
 
@@ -251,9 +258,13 @@ def run_reference(args, rank, world):
     if rank != 0:
         return
     threads = max(1, min(os.cpu_count() or 1, 64))
-    new_tokens = max(2, min(args.steps + 1, GENERATED))
+    batch = args.workload == "batch"
+    # Config 4: the reference serves the requests one after another, so one
+    # request's decode rate (after a 512-token prompt) is its throughput.
+    new_tokens = max(2, min(args.steps + 1, 9 if batch else GENERATED))
     try:
-        value, sample = cpu_reference_decoder(threads, new_tokens, warmup=min(args.warmup, 1))
+        value, sample = cpu_reference_decoder(threads, new_tokens, warmup=min(args.warmup, 1),
+                                              prompt=BATCH_PROMPT if batch else PROMPT)
     except Exception as exc:  # noqa: BLE001
         print(json.dumps({"impl": "reference", "unavailable": f"reference CPU decoder failed: {exc}"}))
         return
@@ -261,7 +272,9 @@ def run_reference(args, rank, world):
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": new_tokens - 1,
         "warmup": args.warmup, "ms_per_step": 1000.0 / value, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic", "impl": "reference",
-        "config": workload_config(1),
+        "config": workload_config(1) if not batch else {
+            "workload": f"config 4 on the reference: {BATCH_SEQUENCES} requests served one after another; "
+                        f"one {BATCH_PROMPT}-token request timed", "global_batch": BATCH_SEQUENCES},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference",
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -438,6 +451,158 @@ def run_ours(args, rank, world, local_rank):
         print(json.dumps(line), flush=True)
 
 
+BATCH_SEQUENCES, BATCH_PROMPT, BATCH_GENERATED = 64, 512, 256  # config 4
+
+
+def run_batch(args, rank, world, local_rank):
+    """Config 4: 64 requests of 512 random prompt ids, 256 greedy tokens
+    each, decoded together (``Decoder(sequences=...)``: one KV cache and
+    position per sequence, every linear over all sequences' rows).  With N
+    ranks the sequences are split over the GPUs (data parallel, full
+    weights per GPU).  One step = one decode token for every sequence; the
+    value is generated tokens/s over the whole job (prefill reported beside
+    it).  Every sequence's tokens equal the single-sequence decoder's and
+    the reference's (tests/test_gpu_decoder_batch.py)."""
+    import torch
+    import torch.distributed as dist
+
+    import leaf_b200 as lq
+    from leaf_b200.decoder import Decoder
+    from leaf_b200.stack import RandomDecoderModel, StackShape
+
+    tp = args.batch_split == "tp" and world > 1
+    if BATCH_SEQUENCES % world:
+        raise SystemExit(f"{BATCH_SEQUENCES} sequences do not split over {world} ranks")
+    seqs = BATCH_SEQUENCES if tp else BATCH_SEQUENCES // world
+    steps = min(args.steps, BATCH_GENERATED - 1)
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    shape = StackShape()
+    model = RandomDecoderModel(shape, seed=1234, device=device)
+    dec = Decoder(model, device=device, sequences=seqs, capacity=BATCH_PROMPT + BATCH_GENERATED,
+                  group=dist.group.WORLD if tp else None)
+    model.release()
+    del model
+    lib = lq.load()
+    stream = torch.cuda.current_stream(device)
+    gen = torch.Generator().manual_seed(7)
+    every = torch.randint(0, shape.vocab, (BATCH_SEQUENCES, BATCH_PROMPT), generator=gen)
+    prompts = every.tolist() if tp else every[rank * seqs:(rank + 1) * seqs].tolist()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    dec.capture_decode()
+
+    def prefill():
+        dec.reset()
+        logits = dec.forward_batch(prompts)
+        lq._lib.check(lib.leafq_argmax(stream.cuda_stream, logits.data_ptr(), seqs, shape.vocab,
+                                       dec._bufs(1)["ids"].data_ptr()))
+
+    prefill()
+    for _ in range(max(args.warmup, 3)):
+        dec._decode_step()
+    torch.cuda.synchronize(device)
+    out_dir = REPO / "gpurun_out"
+    out_dir.mkdir(exist_ok=True)
+    visible = [v for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+    smi_id = visible[local_rank] if local_rank < len(visible) else str(device.index)
+    sampler = ClockSampler(smi_id, out_dir / f"clocks_batch_rank{rank}.csv")
+    time.sleep(0.3)
+    # Prefill (timed on its own), then `steps` decode steps from position 512.
+    barrier()
+    torch.cuda.synchronize(device)
+    p0, p1, d1 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    p0.record(stream)
+    prefill()
+    p1.record(stream)
+    for _ in range(steps):
+        dec._decode_step()
+    d1.record(stream)
+    torch.cuda.synchronize(device)
+    barrier()
+    prefill_ms = max_over_ranks(p0.elapsed_time(p1))
+    decode_ms = max_over_ranks(p1.elapsed_time(d1))
+    # End to end through the public API: generate_batch from host prompts to
+    # host tokens (prompt upload, prefill, every decode step, tokens back).
+    barrier()
+    torch.cuda.synchronize(device)
+    t0 = time.perf_counter()
+    dec.reset()
+    tokens = dec.generate_batch(prompts, steps + 1)
+    torch.cuda.synchronize(device)
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    barrier()
+    time.sleep(0.2)
+    clocks = sampler.stop()
+    status = lib.leafq_device_status()
+    if status != 0:
+        raise RuntimeError(f"device status {status}: {lib.leafq_last_error().decode()}")
+    assert all(len(t) == steps + 1 for t in tokens)
+
+    value = BATCH_SEQUENCES * steps / (decode_ms * 1e-3)
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        h, kv, d, layers = shape.hidden, shape.kv_heads, shape.hidden // shape.heads, shape.layers
+        weight_bytes = (shape.weight_bytes() + shape.scale_bytes()) / (world if tp else 1)
+        mean_keys = BATCH_PROMPT + (steps + 1) / 2
+        kv_bytes = layers * seqs * 2 * kv * d * 4 * mean_keys
+        step_bytes = weight_bytes + kv_bytes
+        ms_step = decode_ms / steps
+        achieved = step_bytes / (ms_step * 1e-3) / 1e9
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            threads = max(1, min(os.cpu_count() or 1, 64))
+            try:
+                cpu_value, sample = cpu_reference_decoder(threads, 9, prompt=BATCH_PROMPT)
+                cpu = {"value": cpu_value, "unit": UNIT, "cores": threads, "kind": "reference",
+                       "sample": sample + "; the reference serves the 64 requests one after another, so "
+                                          "this is its config-4 throughput"}
+            except Exception as exc:  # noqa: BLE001
+                cpu = {"value": None, "unit": UNIT, "cores": threads, "kind": "reference",
+                       "sample": f"failed: {exc}"}
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {
+                "workload": f"config 4: tinyllama-1.1b w8a8, {BATCH_SEQUENCES} sequences x {BATCH_PROMPT}-token "
+                            f"random prompts, greedy decode (one step = one token for every sequence), "
+                            f"positions {BATCH_PROMPT}..{BATCH_PROMPT + steps - 1}",
+                "model": "TinyLlama-1.1B shape (random-init INT8 per-row weights)",
+                "global_batch": BATCH_SEQUENCES, "seq_len": BATCH_PROMPT + BATCH_GENERATED,
+                "parallelism": (f"tp{world} (every linear's rows split over the GPUs, NCCL all-gather of "
+                                f"each output; all {seqs} sequences on every GPU)") if tp else
+                               f"dp{world} ({seqs} sequences per GPU, full weights each)",
+                "l2": "inputs larger than L2 (1.04 GB of weights and the KV caches streamed per step)",
+            },
+            "prefill": {"ms": prefill_ms, "tokens_per_s": BATCH_SEQUENCES * BATCH_PROMPT / (prefill_ms * 1e-3)},
+            "roofline": {
+                "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                "traffic": None, "kernel": "whole decode step (per-operator kernels in one CUDA graph)",
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                "algorithmic_bytes_per_step": step_bytes,
+            },
+            "e2e": {"value": BATCH_SEQUENCES * (steps + 1) / e2e_s, "unit": UNIT,
+                    "h2d_bytes_per_step": int(seqs * BATCH_PROMPT * 4 / (steps + 1)),
+                    "d2h_bytes_per_step": int(seqs * 4),
+                    "note": "generate_batch wall time including the prompt prefill"},
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+            "when": datetime.datetime.now(datetime.timezone.utc).isoformat(timespec="seconds"),
+        }
+        print(json.dumps(line), flush=True)
+
+
 def read_traffic():
     """DRAM bytes per decode step from the committed ncu summary, if any."""
     path = REPO / "profiles" / "decode_model_tinyllama_step.md"
@@ -470,7 +635,10 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     try:
-        run_ours(args, rank, world, local_rank)
+        if args.workload == "batch":
+            run_batch(args, rank, world, local_rank)
+        else:
+            run_ours(args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -294,6 +294,14 @@ int leafq_embed(void* stream, const int32_t* ids, int64_t tokens, const void* ta
  * reference (sum of squares accumulated left to right). */
 int leafq_rmsnorm(void* stream, float* hidden, const float* delta, int add_zero, int64_t tokens,
                   int64_t width, const float* weight, float epsilon, float* out);
+/* leafq_rmsnorm, and the normalised rows quantised in the same pass to
+ * per-token INT8 codes [tokens][width] and scales [tokens] exactly as
+ * leafq_quantize_act quantises them (the input of a W8A8 linear, for
+ * leafq_linear_int_q).  out may be NULL when only the codes are wanted.
+ * Codes need width % 4 == 0, width <= 4096 and 16-byte aligned rows. */
+int leafq_rmsnorm_quantize(void* stream, float* hidden, const float* delta, int add_zero, int64_t tokens,
+                           int64_t width, const float* weight, float epsilon, float* out, int8_t* codes,
+                           float* code_scales);
 /* Host function: RoPE tables [positions][rotary_dim/2] with the reference's
  * float libm calls (frequencies decoder.cpp:929-933, angles :1248-1256). */
 int leafq_rope_tables(float theta, int rotary_dim, int64_t positions, float* cos_out,

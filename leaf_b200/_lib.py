@@ -61,6 +61,7 @@ _SIGNATURES = {
     "leafq_model_plan_destroy": ([_vp], _int),
     "leafq_embed": ([_vp, _vp, _i64, _vp, _vp, _int, _i64, _i64, _i64, _f32, _vp, _vp], _int),
     "leafq_rmsnorm": ([_vp, _vp, _vp, _int, _i64, _i64, _vp, _f32, _vp], _int),
+    "leafq_rmsnorm_quantize": ([_vp, _vp, _vp, _int, _i64, _i64, _vp, _f32, _vp, _vp, _vp], _int),
     "leafq_rope_tables": ([_f32, _int, _i64, _vp, _vp], _int),
     "leafq_rotary_append": ([_vp, _vp, _i64, _int, _int, _int, _int, _vp, _vp, _vp, _vp, _vp, _vp,
                              _i64], _int),

@@ -17,11 +17,7 @@ namespace {
 
 constexpr int kQuantThreads = 256;
 
-__device__ __forceinline__ int8_t code_of(float value, float multiplier) {
-    int r = __float2int_rn(__fmul_rn(value, multiplier));
-    r = r > 127 ? 127 : (r < -128 ? -128 : r);
-    return static_cast<int8_t>(r);
-}
+__device__ __forceinline__ int8_t code_of(float value, float multiplier) { return act_code(value, multiplier); }
 
 __device__ __forceinline__ float block_max(float v, float* scratch) {
     for (int offset = 16; offset > 0; offset >>= 1)

@@ -96,7 +96,7 @@ struct Model {
 
 constexpr size_t kSmemBytes = (size_t)kRingBytes + kMaxCols + kScratchFloats * 4 + 3 * kMaxDim * 4 +
                               2 * (kStageBarriers + 2) * 8 + kStageBarriers * 8 + 2 * 2 * 8 * 4 +
-                              kConsumerWarps * 12 + 64;
+                              kConsumerWarps * 12 + 64 + sizeof(ExpTable) + 8;
 
 __device__ __forceinline__ void consumer_sync() {
     asm volatile("bar.sync 1, %0;" ::"n"(kNC) : "memory");
@@ -270,6 +270,9 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
     int32_t* best_row = reinterpret_cast<int32_t*>(best_v + kConsumerWarps);
     float* total_s = reinterpret_cast<float*>(best_row + kConsumerWarps);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(total_s + 1);
+    // expf's table in shared memory (lanes index it with different k, which
+    // the constant bank would serialise).
+    ExpTable* tab_s = reinterpret_cast<ExpTable*>((reinterpret_cast<uintptr_t>(total_s + 2) + 7) & ~uintptr_t(7));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tid = threadIdx.x;
@@ -283,6 +286,7 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
         *abort_flag = 0;
         fence_barrier_init();
     }
+    if (tid < 32) tab_s->bits[tid] = m.tab.bits[tid];
     const uint32_t tag = *reinterpret_cast<volatile uint32_t*>(m.sync);
     const int32_t id = *reinterpret_cast<volatile int32_t*>(m.ids);
     const int64_t pos = *reinterpret_cast<volatile int32_t*>(m.position);
@@ -450,7 +454,7 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
             float maximum = -INFINITY;
 #pragma unroll
             for (int w = 0; w < kConsumerWarps; ++w) maximum = fmaxf(maximum, partial_max[w]);
-            for (int64_t k = tid; k < keys; k += kNC) scores[k] = expf_libm(__fsub_rn(scores[k], maximum), m.tab);
+            for (int64_t k = tid; k < keys; k += kNC) scores[k] = expf_libm(__fsub_rn(scores[k], maximum), *tab_s);
             consumer_sync();
             if (tid == 0) {
                 float den = 0.0f;
@@ -659,7 +663,7 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
                 group_sync(group);
                 if (ok && live && lane == 0 && (wi & 1) == 0) {
                     const float gate = pb[wi], up = pb[wi + 1];
-                    const float act = __fmul_rn(up, __fdiv_rn(gate, __fadd_rn(1.0f, expf_libm(-gate, m.tab))));
+                    const float act = __fmul_rn(up, __fdiv_rn(gate, __fadd_rn(1.0f, expf_libm(-gate, *tab_s))));
                     store_tagged(op.y_ll + row / 2, act, tag);
                 }
                 continue;

@@ -134,13 +134,93 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(
         out[t * width + c] = __fadd_rn(__fmul_rn(__fmul_rn(row[c], scale), weight[c]), 0.0f);
 }
 
+// The same operator for rows of width % 4 == 0, width <= 4 * 4 * kNormThreads,
+// 16-byte aligned: each thread keeps its (up to 16) values in registers, so
+// the row is read once with all loads in flight.  Optionally the normalised
+// row is quantised to per-token INT8 codes in the same pass (the quantiser
+// of leafq_quantize_act, bit for bit), for a W8A8 linear that follows.
+constexpr int kNormVec = 4;
+
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_vec_kernel(
+    float* __restrict__ hidden, const float* __restrict__ delta, int add_zero, int64_t width,
+    const float* __restrict__ weight, float epsilon, float* __restrict__ out, int8_t* __restrict__ codes,
+    float* __restrict__ code_scales) {
+    extern __shared__ __align__(16) float squares[];  // [width]
+    __shared__ float total;
+    __shared__ float scratch[33];
+    const int64_t t = blockIdx.x;
+    const int n4 = static_cast<int>(width / 4);
+    float4* h4 = reinterpret_cast<float4*>(hidden + t * width);
+    const float4* d4 = delta ? reinterpret_cast<const float4*>(delta + t * width) : nullptr;
+    const float4* w4 = reinterpret_cast<const float4*>(weight);
+    float4 v[kNormVec], w[kNormVec], dv[kNormVec];
+#pragma unroll
+    for (int j = 0; j < kNormVec; ++j) {
+        const int c = threadIdx.x + j * kNormThreads;
+        if (c < n4) {
+            v[j] = h4[c];
+            if (d4) dv[j] = __ldg(d4 + c);
+            w[j] = __ldg(w4 + c);
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < kNormVec; ++j) {
+        const int c = threadIdx.x + j * kNormThreads;
+        if (c < n4) {
+            if (d4) {
+                float4 d = dv[j];
+                if (add_zero) d = make_float4(__fadd_rn(d.x, 0.0f), __fadd_rn(d.y, 0.0f), __fadd_rn(d.z, 0.0f),
+                                              __fadd_rn(d.w, 0.0f));
+                v[j] = make_float4(__fadd_rn(v[j].x, d.x), __fadd_rn(v[j].y, d.y), __fadd_rn(v[j].z, d.z),
+                                   __fadd_rn(v[j].w, d.w));
+                h4[c] = v[j];
+            }
+            reinterpret_cast<float4*>(squares)[c] =
+                make_float4(__fmul_rn(v[j].x, v[j].x), __fmul_rn(v[j].y, v[j].y), __fmul_rn(v[j].z, v[j].z),
+                            __fmul_rn(v[j].w, v[j].w));
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) total = sum_in_order(squares, static_cast<int>(width));
+    __syncthreads();
+    const float scale =
+        __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(width)), epsilon)));
+    float4 o[kNormVec];
+    float absmax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kNormVec; ++j) {
+        const int c = threadIdx.x + j * kNormThreads;
+        if (c < n4) {
+            o[j] = make_float4(__fadd_rn(__fmul_rn(__fmul_rn(v[j].x, scale), w[j].x), 0.0f),
+                               __fadd_rn(__fmul_rn(__fmul_rn(v[j].y, scale), w[j].y), 0.0f),
+                               __fadd_rn(__fmul_rn(__fmul_rn(v[j].z, scale), w[j].z), 0.0f),
+                               __fadd_rn(__fmul_rn(__fmul_rn(v[j].w, scale), w[j].w), 0.0f));
+            if (out) reinterpret_cast<float4*>(out + t * width)[c] = o[j];
+            absmax = fmaxf(absmax, fmaxf(fmaxf(fabsf(o[j].x), fabsf(o[j].y)), fmaxf(fabsf(o[j].z), fabsf(o[j].w))));
+        }
+    }
+    if (!codes) return;  // uniform across the block
+    absmax = block_max(absmax, scratch);
+    const float qscale = fmaxf(__fdiv_rn(absmax, 127.0f), 1e-12f);
+    const float multiplier = __fdiv_rn(1.0f, qscale);
+    if (threadIdx.x == 0) code_scales[t] = qscale;
+    char4* c4 = reinterpret_cast<char4*>(codes + t * width);
+#pragma unroll
+    for (int j = 0; j < kNormVec; ++j) {
+        const int c = threadIdx.x + j * kNormThreads;
+        if (c < n4)
+            c4[c] = make_char4(act_code(o[j].x, multiplier), act_code(o[j].y, multiplier),
+                               act_code(o[j].z, multiplier), act_code(o[j].w, multiplier));
+    }
+}
+
 // ------------------------------------------------------ rotary + KV append
 // Sequence s of a batch owns rows s*tokens .. s*tokens+tokens-1 of qkv, its
 // own cache [kv_heads][capacity][dim] at s * kv_heads * capacity * dim, and
 // its own start position positions[s].  qkv[row] = [q (heads*dim) | k
-// (kv*dim) | v (kv*dim)].  Block (t, s) rotates every q head (to
+// (kv*dim) | v (kv*dim)].  Blocks (t, s, *) rotate every q head (to
 // q_heads[s][head][t]) and k head (to the k cache) of its row and copies v
-// to the v cache.  A position past the cache is recorded in the device
+// to the v cache, spread over blockIdx.z.  A position past the cache is recorded in the device
 // error word and skipped.
 __global__ void rotary_append_kernel(const float* __restrict__ qkv, int64_t tokens, int heads,
                                      int kv_heads, int dim, int rotary_dim,
@@ -163,27 +243,30 @@ __global__ void rotary_append_kernel(const float* __restrict__ qkv, int64_t toke
     const int64_t cache = seq * kv_heads * capacity * dim;
     const float* cs = cos_table + pos * half;
     const float* sn = sin_table + pos * half;
-    // Rotated heads: q heads 0..heads-1, then k heads.
+    // Items of the row, one per thread: a rotation pair or a copied element
+    // of each q / k head, then each v element.
     const int rotated = heads + kv_heads;
-    for (int idx = threadIdx.x; idx < rotated * dim; idx += blockDim.x) {
-        const int head = idx / dim, i = idx - head * dim;
-        if (i >= half && i < rotary_dim) continue;  // written with its pair
+    const int per_head = half + (dim - rotary_dim);
+    const int rot_items = rotated * per_head;
+    const int idx = blockIdx.z * blockDim.x + threadIdx.x;
+    if (idx < rot_items) {
+        const int head = idx / per_head, j = idx - head * per_head;
         const float* src = row + (int64_t)head * dim;
         float* dst = head < heads ? q_heads + ((seq * heads + head) * tokens + t) * dim
                                   : k_cache + cache + ((int64_t)(head - heads) * capacity + pos) * dim;
-        if (i < half) {
-            const float c = cs[i], sv = sn[i];
-            const float a = src[i], b = src[i + half];
-            dst[i] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, sv));
-            dst[i + half] = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, sv));
+        if (j < half) {
+            const float c = cs[j], sv = sn[j];
+            const float a = src[j], b = src[j + half];
+            dst[j] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, sv));
+            dst[j + half] = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, sv));
         } else {
+            const int i = rotary_dim + (j - half);
             dst[i] = src[i];
         }
-    }
-    const float* vsrc = row + (int64_t)rotated * dim;
-    for (int idx = threadIdx.x; idx < kv_heads * dim; idx += blockDim.x) {
-        const int kvh = idx / dim, i = idx - kvh * dim;
-        v_cache[cache + ((int64_t)kvh * capacity + pos) * dim + i] = vsrc[idx];
+    } else if (idx < rot_items + kv_heads * dim) {
+        const int e = idx - rot_items;
+        const int kvh = e / dim, i = e - kvh * dim;
+        v_cache[cache + ((int64_t)kvh * capacity + pos) * dim + i] = row[(int64_t)rotated * dim + e];
     }
 }
 
@@ -204,7 +287,12 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
     const float* __restrict__ q_heads, const float* __restrict__ k_cache,
     const float* __restrict__ v_cache, int64_t tokens, int heads, int kv_heads, int dim,
     const int32_t* __restrict__ positions, int64_t capacity, float scale, float* __restrict__ out,
-    const __grid_constant__ ExpTable tab) {
+    const __grid_constant__ ExpTable tab_g) {
+    // The table in shared memory: lanes index it with different k, which the
+    // constant bank would serialise.
+    __shared__ ExpTable tab;
+    if (threadIdx.x < 32) tab.bits[threadIdx.x] = tab_g.bits[threadIdx.x];
+    __syncthreads();
     extern __shared__ float smem[];
     float* q = smem;
     float* scores = smem + dim;
@@ -260,8 +348,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
 // is staged in shared memory once for all of them (coalesced loads; the next
 // chunk is loaded into registers while the current one is used).
 //   dots:  thread (h, k) of a chunk of min(64, kGroupThreads / group) keys,
-//          its dot over d in order (rows padded to DIM + 1 floats: no bank
-//          conflicts);
+//          its dot over d in order, the query in registers (key rows padded
+//          to DIM + 4 floats: conflict-free float4 reads);
 //   softmax: exponentials by all threads, one thread per head for the
 //          denominator in key order, division by all threads;
 //   values: thread (h, d), its sum over keys in order.
@@ -286,12 +374,18 @@ __global__ void __launch_bounds__(kGroupThreads) attention_group_kernel(
     const float* __restrict__ q_heads, const float* __restrict__ k_cache,
     const float* __restrict__ v_cache, int64_t tokens, int heads, int kv_heads,
     const int32_t* __restrict__ positions, int64_t capacity, float scale, float* __restrict__ out,
-    const __grid_constant__ ExpTable tab) {
+    const __grid_constant__ ExpTable tab_g) {
+    // The table in shared memory: lanes index it with different k, which the
+    // constant bank would serialise.
+    __shared__ ExpTable tab;
+    if (threadIdx.x < 32) tab.bits[threadIdx.x] = tab_g.bits[threadIdx.x];
+    __syncthreads();
     constexpr int kRowF4 = DIM / 4;
     constexpr int kF4 = (kGroupRows * kRowF4 + kGroupThreads - 1) / kGroupThreads;
     extern __shared__ __align__(16) float scores[];
     __shared__ float q_s[kGroupMaxHeads * DIM];
-    __shared__ __align__(16) float rows_s[kGroupRows * (DIM + 1)];
+    constexpr int kLd = DIM + 4;  // padded key row: 16-byte aligned, conflict-free float4 reads
+    __shared__ __align__(16) float rows_s[kGroupRows * kLd];
     __shared__ float red[kGroupThreads / 32];
     __shared__ float max_s[kGroupMaxHeads], den_s[kGroupMaxHeads];
     const int group = heads / kv_heads;
@@ -310,6 +404,14 @@ __global__ void __launch_bounds__(kGroupThreads) attention_group_kernel(
     const float* kbase = k_cache + cache;
     const float* vbase = v_cache + cache;
     const int tid = threadIdx.x;
+    if (tid < 2) {
+        // The whole key (thread 0) or value (thread 1) range into L2 now, so
+        // the chunk loads below wait on L2 rather than on HBM.
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(tid == 0 ? kbase : vbase);
+        const int64_t bytes = keys * DIM * static_cast<int64_t>(sizeof(float));
+        for (int64_t off = 0; off < bytes; off += 32768)
+            bulk_prefetch_l2(src + off, static_cast<uint32_t>(min64(32768, bytes - off)));
+    }
     for (int i = tid; i < group * DIM; i += kGroupThreads) {
         const int h = i / DIM, d = i % DIM;
         q_s[i] = q_heads[((seq * heads + kvh * group + h) * tokens + t) * DIM + d];
@@ -317,6 +419,10 @@ __global__ void __launch_bounds__(kGroupThreads) attention_group_kernel(
     // ---- dots
     const int my_h = tid / chunk, my_k = tid % chunk;
     const bool dotter = my_h < group;
+    __syncthreads();
+    float q[DIM];
+#pragma unroll
+    for (int d = 0; d < DIM; ++d) q[d] = q_s[(dotter ? my_h : 0) * DIM + d];
     float4 pre[kF4];
     fetch_rows<DIM>(pre, kbase, static_cast<int>(min64(chunk, keys)));
     float local_max = -INFINITY;
@@ -326,20 +432,23 @@ __global__ void __launch_bounds__(kGroupThreads) attention_group_kernel(
 #pragma unroll
         for (int j = 0; j < kF4; ++j) {
             const int i = tid + j * kGroupThreads;
-            if (i < n * kRowF4) {
-                float* dst = rows_s + (i / kRowF4) * (DIM + 1) + (i % kRowF4) * 4;
-                dst[0] = pre[j].x, dst[1] = pre[j].y, dst[2] = pre[j].z, dst[3] = pre[j].w;
-            }
+            if (i < n * kRowF4)
+                *reinterpret_cast<float4*>(rows_s + (i / kRowF4) * kLd + (i % kRowF4) * 4) = pre[j];
         }
         __syncthreads();
         if (c0 + chunk < keys)
             fetch_rows<DIM>(pre, kbase + (c0 + chunk) * DIM, static_cast<int>(min64(chunk, keys - c0 - chunk)));
         if (dotter && my_k < n) {
-            const float* kr = rows_s + my_k * (DIM + 1);
-            const float* qh = q_s + my_h * DIM;
+            const float* kr = rows_s + my_k * kLd;
             float dot = 0.0f;
 #pragma unroll
-            for (int d = 0; d < DIM; ++d) dot = __fadd_rn(dot, __fmul_rn(qh[d], kr[d]));
+            for (int d = 0; d < DIM; d += 4) {
+                const float4 k4 = *reinterpret_cast<const float4*>(kr + d);
+                dot = __fadd_rn(dot, __fmul_rn(q[d], k4.x));
+                dot = __fadd_rn(dot, __fmul_rn(q[d + 1], k4.y));
+                dot = __fadd_rn(dot, __fmul_rn(q[d + 2], k4.z));
+                dot = __fadd_rn(dot, __fmul_rn(q[d + 3], k4.w));
+            }
             const float sc = __fmul_rn(__fmul_rn(dot, scale), scale);
             scores[my_h * ld + c0 + my_k] = sc;
             local_max = fmaxf(local_max, sc);
@@ -439,7 +548,12 @@ __global__ void __launch_bounds__(kTileThreads, 3) attention_tile_kernel(
     const float* __restrict__ q_heads, const float* __restrict__ k_cache,
     const float* __restrict__ v_cache, int sequences, int64_t tokens, int heads, int kv_heads,
     const int32_t* __restrict__ positions, int64_t capacity, int64_t max_keys, float scale,
-    float* __restrict__ out, float* __restrict__ workspace, const __grid_constant__ ExpTable tab) {
+    float* __restrict__ out, float* __restrict__ workspace, const __grid_constant__ ExpTable tab_g) {
+    // The table in shared memory: lanes index it with different k, which the
+    // constant bank would serialise.
+    __shared__ ExpTable tab;
+    if (threadIdx.x < 32) tab.bits[threadIdx.x] = tab_g.bits[threadIdx.x];
+    __syncthreads();
     __shared__ __align__(16) float rows_s[kTileKeys * DIM];
     const int group = heads / kv_heads;
     const int tq = kTileThreads / group;
@@ -571,7 +685,12 @@ __device__ __forceinline__ float silu_gate_one(float g, float u, const ExpTable&
 // Outputs are consecutive in memory (out [tokens][width] row-major and
 // gate_up its interleaved pairs), so the flat index i covers every token.
 __global__ void silu_gate_kernel(const float* __restrict__ gate_up, int64_t tokens, int64_t width,
-                                 float* __restrict__ out, int vec, const __grid_constant__ ExpTable tab) {
+                                 float* __restrict__ out, int vec, const __grid_constant__ ExpTable tab_g) {
+    // The table in shared memory: lanes index it with different k, which the
+    // constant bank would serialise.
+    __shared__ ExpTable tab;
+    if (threadIdx.x < 32) tab.bits[threadIdx.x] = tab_g.bits[threadIdx.x];
+    __syncthreads();
     const int64_t n = tokens * width;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     const int64_t first = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -639,7 +758,12 @@ __global__ void advance_kernel(int32_t* positions, int sequences, int32_t count)
 }
 
 __global__ void expf_kernel(const float* __restrict__ x, int64_t n, float* __restrict__ y,
-                            const __grid_constant__ ExpTable tab) {
+                            const __grid_constant__ ExpTable tab_g) {
+    // The table in shared memory: lanes index it with different k, which the
+    // constant bank would serialise.
+    __shared__ ExpTable tab;
+    if (threadIdx.x < 32) tab.bits[threadIdx.x] = tab_g.bits[threadIdx.x];
+    __syncthreads();
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x)
         y[i] = expf_libm(x[i], tab);
@@ -672,24 +796,49 @@ int leafq_embed(void* stream, const int32_t* ids, int64_t tokens, const void* ta
                   vocab, hidden, embedding_scale, out, error_flag);
 }
 
-int leafq_rmsnorm(void* stream, float* hidden, const float* delta, int add_zero, int64_t tokens,
-                  int64_t width, const float* weight, float epsilon, float* out) {
+int leafq_rmsnorm_quantize(void* stream, float* hidden, const float* delta, int add_zero, int64_t tokens,
+                           int64_t width, const float* weight, float epsilon, float* out, int8_t* codes,
+                           float* code_scales) {
     clear_error();
     if (tokens < 0 || width <= 0 || width > 16384 || tokens > 0x7fffffff) {
         set_error("leafq_rmsnorm: width must be 1..16384");
         return LEAFQ_ERR_INVALID;
     }
     if (tokens == 0) return LEAFQ_OK;
-    if (!hidden || !weight || !out) {
+    if (!hidden || !weight || (!out && !codes) || (codes && !code_scales)) {
         set_error("leafq_rmsnorm: null pointer");
         return LEAFQ_ERR_INVALID;
     }
-    const size_t smem = 2 * static_cast<size_t>(width) * sizeof(float);
-    int st = allow_smem(reinterpret_cast<const void*>(rmsnorm_kernel), smem, "rmsnorm");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const bool vec = width % 4 == 0 && width <= 4 * kNormVec * kNormThreads && aligned16(hidden) &&
+                     (!delta || aligned16(delta)) && aligned16(weight) && (!out || aligned16(out)) &&
+                     (!codes || reinterpret_cast<uintptr_t>(codes) % 4 == 0);
+    const size_t smem = static_cast<size_t>(width) * sizeof(float);
+    if (vec) {
+        int st = allow_smem(reinterpret_cast<const void*>(rmsnorm_vec_kernel), smem, "rmsnorm");
+        if (st) return st;
+        return launch(rmsnorm_vec_kernel, dim3(static_cast<unsigned>(tokens)), dim3(kNormThreads), smem, s, false,
+                      "rmsnorm", hidden, delta, add_zero, width, weight, epsilon, out, codes, code_scales);
+    }
+    if (codes) {
+        set_error("leafq_rmsnorm_quantize: codes need width % 4 == 0, width <= 4096 and aligned rows");
+        return LEAFQ_ERR_UNSUPPORTED;
+    }
+    int st = allow_smem(reinterpret_cast<const void*>(rmsnorm_kernel), 2 * smem, "rmsnorm");
     if (st) return st;
-    return launch(rmsnorm_kernel, dim3(static_cast<unsigned>(tokens)), dim3(kNormThreads), smem,
-                  static_cast<cudaStream_t>(stream), false, "rmsnorm", hidden, delta, add_zero, width,
-                  weight, epsilon, out);
+    return launch(rmsnorm_kernel, dim3(static_cast<unsigned>(tokens)), dim3(kNormThreads), 2 * smem, s, false,
+                  "rmsnorm", hidden, delta, add_zero, width, weight, epsilon, out);
+}
+
+int leafq_rmsnorm(void* stream, float* hidden, const float* delta, int add_zero, int64_t tokens,
+                  int64_t width, const float* weight, float epsilon, float* out) {
+    if (!out) {
+        clear_error();
+        set_error("leafq_rmsnorm: null pointer");
+        return LEAFQ_ERR_INVALID;
+    }
+    return leafq_rmsnorm_quantize(stream, hidden, delta, add_zero, tokens, width, weight, epsilon, out, nullptr,
+                                  nullptr);
 }
 
 int leafq_rope_tables(float theta, int rotary_dim, int64_t positions, float* cos_out,
@@ -729,7 +878,9 @@ int leafq_rotary_append_batch(void* stream, const float* qkv, int sequences, int
         set_error("leafq_rotary_append: null pointer");
         return LEAFQ_ERR_INVALID;
     }
-    return launch(rotary_append_kernel, dim3(static_cast<unsigned>(tokens), static_cast<unsigned>(sequences)),
+    const int items = (heads + kv_heads) * (rotary_dim / 2 + dim - rotary_dim) + kv_heads * dim;
+    return launch(rotary_append_kernel,
+                  dim3(static_cast<unsigned>(tokens), static_cast<unsigned>(sequences), (items + 255) / 256),
                   dim3(256), 0, static_cast<cudaStream_t>(stream), false, "rotary_append", qkv,
                   tokens, heads, kv_heads, dim, rotary_dim, cos_table, sin_table, positions, q_heads,
                   k_cache, v_cache, capacity);

@@ -112,6 +112,17 @@ gemm_w8a8_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
         // ------------------------------------------------ TMA producer
         if (elect_one_sync()) {
             const uint64_t keep = l2_policy_evict_last();
+            // The weights do not depend on the previous kernel: the first
+            // tile's first stages of weight rows are requested before waiting
+            // for it (with programmatic dependent launch this overlaps its tail).
+            const int early = blockIdx.x < tiles ? (kblocks < kStages ? kblocks : kStages) : 0;
+            {
+                const int n0 = (blockIdx.x / a.m_tiles) * BN;
+                for (int kb = 0; kb < early; ++kb) {
+                    mbar_arrive_expect_tx(&full[kb], kABytes + kBBytes);
+                    tma_load_2d(b_tiles + (size_t)kb * kBBytes, &map_w, kb * BK, n0, &full[kb], keep);
+                }
+            }
             grid_dependency_wait();  // the codes come from the previous kernel
             int it = 0;
             bool ok = true;
@@ -120,6 +131,10 @@ gemm_w8a8_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
                 const int n0 = (tile / a.m_tiles) * BN;
                 for (int kb = 0; kb < kblocks; ++kb, ++it) {
                     const int s = it % kStages;
+                    if (it < early) {  // weights already requested
+                        tma_load_2d(a_tiles + (size_t)s * kABytes, &map_q, kb * BK, m0, &full[s], keep);
+                        continue;
+                    }
                     if (it >= kStages && !mbar_wait(&empty[s], ((it / kStages) - 1) & 1, kSiteGemmEmpty)) {
                         ok = false;
                         break;

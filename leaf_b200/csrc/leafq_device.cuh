@@ -192,6 +192,14 @@ __device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c
 __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
 __device__ __forceinline__ int64_t max64(int64_t a, int64_t b) { return a > b ? a : b; }
 
+// Per-token dynamic INT8 code (decoder.cpp:618-627): round half to even of
+// value * multiplier, saturated; multiplier = 1 / max(absmax / 127, 1e-12).
+__device__ __forceinline__ int8_t act_code(float value, float multiplier) {
+    int r = __float2int_rn(__fmul_rn(value, multiplier));
+    r = r > 127 ? 127 : (r < -128 ? -128 : r);
+    return static_cast<int8_t>(r);
+}
+
 // --------------------------------------------------------------- tcgen05
 __device__ __forceinline__ void tmem_alloc(uint32_t* smem_result, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(

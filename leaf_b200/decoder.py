@@ -28,7 +28,7 @@ import numpy as np
 import torch
 
 from . import _lib
-from ._lib import LeafError, check, load
+from ._lib import LEAFQ_FLAG_PDL, LeafError, check, load
 from .artifact import Artifact, HostTensor
 from .linear import QuantWeight, Workspace
 
@@ -67,7 +67,7 @@ def _concat_rows(parts: list[HostTensor], device: torch.device, interleave: bool
 
 class Decoder:
     def __init__(self, artifact, activation_bits: int = 8, device="cuda",
-                 capacity: Optional[int] = None, sequences: int = 1):
+                 capacity: Optional[int] = None, sequences: int = 1, group=None):
         """artifact: a path, an ``Artifact``, or any object with the same
         ``config`` / ``get(name)`` interface whose payloads are tensors
         (``leaf_b200.stack.RandomDecoderModel``).
@@ -77,7 +77,15 @@ class Decoder:
         rows): ``forward_batch`` / ``generate_batch`` give each sequence the
         tokens the single-sequence decoder gives it, bit for bit -- the
         reference serves the same requests one after another
-        (main_decoder.cpp:233-300)."""
+        (main_decoder.cpp:233-300).
+
+        group: a torch.distributed process group of one process per GPU.
+        Every linear's weight is then split by output rows over the group
+        (rank r keeps rows [r*N/G, (r+1)*N/G)), each rank computes its rows
+        and the slices are all-gathered (NCCL) into the full output on every
+        rank; the other operators run on every rank.  Rows are independent,
+        so the results are the unsharded ones bit for bit.  Every rank must
+        make the same calls."""
         art = artifact if hasattr(artifact, "get") else Artifact(artifact)
         cfg = art.config
         if not (cfg.norm_kind == 0 and cfg.position_kind == 0 and cfg.gated == 1 and
@@ -92,6 +100,14 @@ class Decoder:
             raise LeafError(_lib.LEAFQ_ERR_INVALID, "sequences must be positive")
         self.cfg = cfg
         self.sequences = int(sequences)
+        self.group = group
+        if group is not None:
+            import torch.distributed as dist
+            self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        else:
+            self.world, self.rank = 1, 0
+        self._full_rows: dict[int, int] = {}
+        self._gather_bufs: dict = {}
         self.activation_bits = activation_bits
         self.device = torch.device(device)
         self.capacity = int(capacity or cfg.max_positions)
@@ -102,7 +118,7 @@ class Decoder:
             return _on(t.data, dev).to(torch.float32).reshape(-1).contiguous()
 
         def weight(parts, interleave=False):
-            return _concat_rows(parts, dev, interleave)
+            return self._shard(_concat_rows(parts, dev, interleave))
 
         emb = art.get("model.embed_tokens.weight")
         self.embed_table = _on(emb.data, dev).contiguous()
@@ -151,6 +167,7 @@ class Decoder:
         self.step_logits = torch.zeros(cfg.vocab, dtype=torch.float32, device=dev)
         self._plan = None
         self._plan_refs = None
+        self._step_ready = False
 
     # ------------------------------------------------------------ buffers
     def _bufs(self, tokens: int) -> dict:
@@ -168,7 +185,9 @@ class Decoder:
                      q_heads=e(S, c.heads, tokens, c.head_dim), attn=e(rows, q), o=e(rows, c.hidden),
                      gate_up=e(rows, 2 * c.intermediate), act=e(rows, c.intermediate),
                      down=e(rows, c.hidden), last=e(S, c.hidden), logits=e(S, c.vocab),
-                     workspace=Workspace(dev))
+                     workspace=Workspace(dev),
+                     codes=torch.empty((rows, c.hidden), dtype=torch.int8, device=dev),
+                     code_scales=e(rows))
             # Each chunk size owns its workspace, sized once: a captured graph
             # keeps its pointers, so nothing it uses may be reallocated.
             for w in self._weights():
@@ -188,7 +207,50 @@ class Decoder:
             yield from (layer["qkv"], layer["o"], layer["gate_up"], layer["down"])
         yield self.lm_head
 
+    # ------------------------------------------------------- row sharding
+    def _shard(self, w: QuantWeight) -> QuantWeight:
+        """This rank's rows of a weight (the whole weight without a group)."""
+        if self.world == 1:
+            return w
+        from .parallel import RowShards
+
+        part = RowShards(w.rows, self.world)
+        if not part.even:
+            raise LeafError(_lib.LEAFQ_ERR_UNSUPPORTED,
+                            f"{w.rows} rows do not split evenly over {self.world} ranks")
+        b, e = part.begin(self.rank), part.end(self.rank)
+        shard = QuantWeight(w.data[b:e].clone(), None if w.scales is None else w.scales[b:e].clone(), e - b,
+                            w.cols, w.bits, w.group)
+        self._full_rows[id(shard)] = w.rows
+        return shard
+
+    def _sharded_out(self, w: QuantWeight, out: torch.Tensor, tokens: int):
+        """(buffer this rank's rows are written to, gather step or None)."""
+        if self.world == 1:
+            return out, None
+        n = w.rows
+        key = (tokens, n)
+        bufs = self._gather_bufs.get(key)
+        if bufs is None:
+            local = torch.empty((tokens, n), dtype=torch.float32, device=self.device)
+            stacked = torch.empty((self.world, tokens, n), dtype=torch.float32, device=self.device)
+            bufs = self._gather_bufs[key] = (local, stacked)
+        local, stacked = bufs
+
+        def gather():
+            import torch.distributed as dist
+
+            if tokens == 1:  # [world][n] is already the row order of [1, world * n]
+                dist.all_gather_into_tensor(out.view(-1), local.view(-1), group=self.group)
+            else:
+                dist.all_gather_into_tensor(stacked.view(-1), local.view(-1), group=self.group)
+                out.view(tokens, self.world, n).copy_(stacked.permute(1, 0, 2))
+        return local, gather
+
     # -------------------------------------------------------------- ops
+    # Linears are launched with programmatic dependent launch: their kernels
+    # wait on the previous kernel before reading its output, and start
+    # streaming weights (which nothing in the step writes) before that.
     def _linear(self, x: torch.Tensor, w: QuantWeight, out: torch.Tensor, tokens: int,
                 workspace: Workspace) -> None:
         lib = self.lib
@@ -196,11 +258,14 @@ class Decoder:
         ws = workspace.buffer if need else None
         if ws is not None and ws.numel() < need:
             raise LeafError(_lib.LEAFQ_ERR_INVALID, "decoder workspace too small")
+        dst, gather = self._sharded_out(w, out, tokens)
         check(lib.leafq_linear(_stream(), x.data_ptr(), tokens, w.cols, w.data.data_ptr(),
                                None if w.scales is None else w.scales.data_ptr(), w.rows, w.bits,
-                               w.group, self.activation_bits, None, out.data_ptr(),
+                               w.group, self.activation_bits, None, dst.data_ptr(),
                                None if ws is None else ws.data_ptr(), 0 if ws is None else ws.numel(),
-                               0))
+                               LEAFQ_FLAG_PDL))
+        if gather is not None:
+            gather()
 
     def _forward_device(self, b: dict, tokens: int) -> None:
         """One forward of `tokens` ids per sequence already in b["ids"] at
@@ -214,12 +279,37 @@ class Decoder:
                               self.embed_bits, self.embed_group, c.vocab, c.hidden,
                               ctypes.c_float(c.embedding_scale), b["hidden"].data_ptr(),
                               self.error_flag.data_ptr()))
-        check(lib.leafq_rmsnorm(s, b["hidden"].data_ptr(), None, 0, rows, c.hidden,
-                                self.layers[0]["input_norm"].data_ptr(), ctypes.c_float(c.epsilon),
-                                b["normalized"].data_ptr()))
+        # With more than 8 rows the W8A8 linears take codes: the RMSNorm
+        # before q|k|v and gate|up quantises its output in the same pass
+        # (leafq_rmsnorm_quantize), which is what leafq_linear's own
+        # quantiser would produce from the fp32 rows.
+        fuse = self.activation_bits == 8 and rows > 8 and c.hidden % 4 == 0 and c.hidden <= 4096
+
+        def norm(delta, add_zero, weight, codes):
+            d = None if delta is None else delta.data_ptr()
+            if codes:
+                check(lib.leafq_rmsnorm_quantize(s, b["hidden"].data_ptr(), d, add_zero, rows, c.hidden,
+                                                 weight.data_ptr(), ctypes.c_float(c.epsilon), None,
+                                                 b["codes"].data_ptr(), b["code_scales"].data_ptr()))
+            else:
+                check(lib.leafq_rmsnorm(s, b["hidden"].data_ptr(), d, add_zero, rows, c.hidden,
+                                        weight.data_ptr(), ctypes.c_float(c.epsilon), b["normalized"].data_ptr()))
+
+        def normed_linear(w, out):
+            if fuse:
+                dst, gather = self._sharded_out(w, out, rows)
+                check(lib.leafq_linear_int_q(s, b["codes"].data_ptr(), b["code_scales"].data_ptr(), rows, w.cols,
+                                             w.data.data_ptr(), w.scales.data_ptr(), w.rows, w.bits, w.group,
+                                             None, dst.data_ptr(), None, LEAFQ_FLAG_PDL))
+                if gather is not None:
+                    gather()
+            else:
+                self._linear(b["normalized"], w, out, rows, b["workspace"])
+
+        norm(None, 0, self.layers[0]["input_norm"], fuse)
         ws = b["attention_ws"]
         for i, layer in enumerate(self.layers):
-            self._linear(b["normalized"], layer["qkv"], b["qkv"], rows, b["workspace"])
+            normed_linear(layer["qkv"], b["qkv"])
             check(lib.leafq_rotary_append_batch(s, b["qkv"].data_ptr(), S, tokens, c.heads, c.kv_heads,
                                                 c.head_dim, c.rotary_dim, self.cos.data_ptr(),
                                                 self.sin.data_ptr(), self.position.data_ptr(),
@@ -231,21 +321,16 @@ class Decoder:
                                             self.capacity, ctypes.c_float(self.scale), b["attn"].data_ptr(),
                                             ws.data_ptr(), ws.numel()))
             self._linear(b["attn"], layer["o"], b["o"], rows, b["workspace"])
-            check(lib.leafq_rmsnorm(s, b["hidden"].data_ptr(), b["o"].data_ptr(), 0, rows, c.hidden,
-                                    layer["post_norm"].data_ptr(), ctypes.c_float(c.epsilon),
-                                    b["normalized"].data_ptr()))
-            self._linear(b["normalized"], layer["gate_up"], b["gate_up"], rows, b["workspace"])
+            norm(b["o"], 0, layer["post_norm"], fuse)
+            normed_linear(layer["gate_up"], b["gate_up"])
             check(lib.leafq_silu_gate(s, b["gate_up"].data_ptr(), rows, c.intermediate,
                                       b["act"].data_ptr()))
             self._linear(b["act"], layer["down"], b["down"], rows, b["workspace"])
             last = i + 1 == len(self.layers)
-            norm = (self.layers[i + 1]["input_norm"] if not last else self.final_norm)
-            if norm is not None:
-                check(lib.leafq_rmsnorm(s, b["hidden"].data_ptr(), b["down"].data_ptr(), 1, rows,
-                                        c.hidden, norm.data_ptr(), ctypes.c_float(c.epsilon),
-                                        b["normalized"].data_ptr()))
-            else:  # no final norm: the logits read the residual stream itself
+            if last and self.final_norm is None:
+                # no final norm: the logits would read the residual stream itself
                 raise LeafError(_lib.LEAFQ_ERR_UNSUPPORTED, "artifacts without a final norm")
+            norm(b["down"], 1, self.final_norm if last else self.layers[i + 1]["input_norm"], fuse and not last)
         if tokens == 1:
             last_rows = b["normalized"]
         elif S == 1:
@@ -281,9 +366,25 @@ class Decoder:
         self.length += len(ids)
         return b["logits"]
 
+    def _decode_step(self) -> None:
+        """One decode step of every sequence from the ids of the previous
+        argmax (the captured graph, or its launches when not captured)."""
+        if self.graph is not None:
+            self.graph.replay()
+            return
+        b = self._bufs(1)
+        self._forward_device(b, 1)
+        check(self.lib.leafq_argmax(_stream(), b["logits"].data_ptr(), self.sequences, self.cfg.vocab,
+                                    b["ids"].data_ptr()))
+
     def capture_decode(self) -> None:
         """Capture one decode step (ids from the previous step's argmax) as
-        a CUDA graph."""
+        a CUDA graph.  A sharded decoder steps without a graph (its NCCL
+        gathers run eagerly)."""
+        if self.world > 1:
+            self._bufs(1)
+            self._step_ready = True
+            return
         b = self._bufs(1)
         stream = torch.cuda.Stream(self.device)
         stream.wait_stream(torch.cuda.current_stream(self.device))
@@ -301,11 +402,12 @@ class Decoder:
             check(self.lib.leafq_argmax(_stream(), b["logits"].data_ptr(), self.sequences, self.cfg.vocab,
                                         b["ids"].data_ptr()))
         self.graph = graph
+        self._step_ready = True
 
     def generate(self, prompt, max_new: int) -> list[int]:
         """main_decoder.cpp:95-113 greedy continuation without EOS handling
         on the device: prefill, then one graph replay per further token."""
-        if self.graph is None:
+        if not self._step_ready:
             self.capture_decode()
         if self.length + len(prompt) + max_new - 1 > min(self.cfg.max_positions, self.capacity):
             raise LeafError(_lib.LEAFQ_ERR_INVALID, "context length exceeds artifact limit")
@@ -321,7 +423,7 @@ class Decoder:
             if eos and int(out[i - 1].item()) in eos:
                 produced = i
                 break
-            self.graph.replay()
+            self._decode_step()
             self.length += 1
             out[i:i + 1].copy_(step["ids"])
         return [int(t) for t in out[:produced].tolist()]
@@ -354,7 +456,7 @@ class Decoder:
         computed with the batch and dropped), as the reference's loop does."""
         if max_new < 1:
             raise LeafError(_lib.LEAFQ_ERR_INVALID, "max_new must be positive")
-        if self.graph is None:
+        if not self._step_ready:
             self.capture_decode()
         tokens = len(prompts[0]) if prompts else 0
         if self.length + tokens + max_new - 1 > min(self.cfg.max_positions, self.capacity):
@@ -366,7 +468,7 @@ class Decoder:
         out = torch.empty((max_new, self.sequences), dtype=torch.int32, device=self.device)
         out[0].copy_(step["ids"])
         for i in range(1, max_new):
-            self.graph.replay()
+            self._decode_step()
             out[i].copy_(step["ids"])
         self.length += max_new - 1
         eos = set(self.cfg.eos_tokens)
@@ -384,7 +486,8 @@ class Decoder:
         """The one-launch decode step needs per-row INT8 weights and
         embedding, W8A8, and a cache of at most 4096 rows."""
         per_row = all(w.bits == 8 and w.group == w.cols for w in self._weights())
-        return (per_row and self.sequences == 1 and self.activation_bits == 8 and self.embed_bits == 8 and
+        return (per_row and self.sequences == 1 and self.world == 1 and self.activation_bits == 8 and
+                self.embed_bits == 8 and
                 self.embed_group == self.cfg.hidden and self.capacity <= 4096 and
                 self.final_norm is not None)
 

@@ -62,6 +62,17 @@ def test_rmsnorm_bit_exact(cuda_device, kind, width):
             expect = od.rmsnorm(hx, w, 1e-5)
         got = out.cpu().numpy()
         assert np.array_equal(got.view(np.uint32), expect.view(np.uint32)), kind
+        if width % 4 == 0 and kind != "huge":
+            # The same norm with the per-token INT8 quantisation fused in.
+            h = torch.from_numpy(x).cuda()
+            codes = torch.empty((rows, width), dtype=torch.int8, device="cuda")
+            sx = torch.empty(rows, device="cuda")
+            lq._lib.check(lq.load().leafq_rmsnorm_quantize(
+                _s(), h.data_ptr(), d.data_ptr(), add_zero, rows, width, torch.from_numpy(w).cuda().data_ptr(),
+                ctypes.c_float(1e-5), None, codes.data_ptr(), sx.data_ptr()))
+            eq, esx = oracle.quantize_act(expect)
+            assert np.array_equal(codes.cpu().numpy(), eq), kind
+            assert np.array_equal(sx.cpu().numpy().view(np.uint32), esx.view(np.uint32)), kind
 
 
 def test_rotary_attention_silu_bit_exact(cuda_device):

@@ -121,3 +121,71 @@ def test_sharded_linear_two_gpus():
         errors.append(failures.get())
     assert not errors, errors
     assert all(p.exitcode == 0 for p in procs)
+
+
+def _decoder_rank_main(rank, world, port, path, prompts, new_tokens, failures, results):
+    import torch.distributed as dist
+
+    from leaf_b200.decoder import Decoder
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        dec = Decoder(path, sequences=len(prompts), group=dist.group.WORLD)
+        got = dec.generate_batch(prompts, new_tokens)
+        if dec.device_status() != 0:
+            failures.put(f"rank {rank}: device status")
+        results.put((rank, got))
+    except Exception as exc:  # noqa: BLE001
+        failures.put(f"rank {rank}: {exc!r}")
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_decoder_two_gpus(tmp_path):
+    """The batched decoder with every linear's rows split over 2 GPUs (NCCL
+    all-gather of each output): every sequence's tokens equal the unsharded
+    decoder's, and the first is the reference's recorded request."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import decoder_fixture as fx  # tests/golden
+    from test_gpu_decoder import _artifact
+    from leaf_b200.decoder import Decoder
+
+    path, golden = _artifact(tmp_path, "tiny_w8", fx.TINY)
+    generated = golden["generated"].tolist()
+    rng = np.random.default_rng(21)
+    prompt = golden["prompt"].tolist()
+    prompts = [prompt] + [rng.integers(0, fx.TINY.vocab, size=len(prompt)).tolist() for _ in range(2)]
+    expect = Decoder(path, sequences=3).generate_batch(prompts, len(generated))
+    assert expect[0] == generated
+    ctx = torch.multiprocessing.get_context("spawn")
+    failures, results = ctx.Queue(), ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_decoder_rank_main,
+                         args=(r, 2, port, str(path), prompts, len(generated), failures, results))
+             for r in range(2)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in range(2):
+        try:
+            rank, tokens = results.get(timeout=300)
+            got[rank] = tokens
+        except Exception:  # noqa: BLE001
+            break
+    for p in procs:
+        p.join(timeout=60)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    errors = []
+    while not failures.empty():
+        errors.append(failures.get())
+    assert not errors, errors
+    assert not alive, "a rank did not finish"
+    assert got.get(0) == expect and got.get(1) == expect
