@@ -89,6 +89,23 @@ int leafq_linear(void* stream, const float* x, int64_t tokens, int64_t cols, con
                  int activation_bits, const float* bias, float* y, void* workspace,
                  size_t workspace_bytes, uint32_t flags);
 
+/* Decoder::Impl::linear for a weight that has a calibrated `input_scale`
+ * tensor (SmoothQuant, decoder.cpp:1008-1019): x[t][c] * input_scale[c]
+ * (one float rounding) is what gets quantised (activation_bits 8, the
+ * scaling fused into the quantiser) or multiplied (activation_bits 32).
+ * input_scale NULL is leafq_linear.  workspace: at least
+ * leafq_linear_smooth_workspace_bytes(tokens, cols, activation_bits) bytes,
+ * 256-byte aligned. */
+size_t leafq_linear_smooth_workspace_bytes(int64_t tokens, int64_t cols, int activation_bits);
+/* y[t][c] = x[t][c] * col_scale[c]: the SmoothQuant scaling alone (for a
+ * caller that quantises elsewhere, e.g. before a sharded linear). */
+int leafq_scale_columns(void* stream, const float* x, int64_t tokens, int64_t cols, const float* col_scale,
+                        float* y);
+int leafq_linear_smooth(void* stream, const float* x, const float* input_scale, int64_t tokens, int64_t cols,
+                        const void* weight, const float* weight_scales, int64_t rows, int bits, int64_t group,
+                        int activation_bits, const float* bias, float* y, void* workspace,
+                        size_t workspace_bytes, uint32_t flags);
+
 /* Integer linear from codes already produced by leafq_quantize_act (or by
  * the reference's quantiser).  acc, when not NULL, receives every int32
  * group sum, layout [tokens, rows, cols / group]: the accumulator the
@@ -115,6 +132,22 @@ int leafq_graph_quantize(void* stream, const float* x, int64_t count, float scal
 int leafq_gemm_i8_per_channel(void* stream, const int8_t* a, const int8_t* b, const float* bias,
                               float input_scale, const float* weight_scales, float* out,
                               int64_t m, int64_t k, int64_t n, int activation);
+
+/* A quantised Gemm / MatMul node of the graph executor, execute_quant_linear
+ * (executor.cpp:524-614): a fp32 [m, k] ([k, m] with trans_a, Gemm only),
+ * statically quantised with input_scale (as leafq_graph_quantize); weight
+ * int8 [k, n] ([n, k] with trans_b); out fp32 [m, n] =
+ * act(alpha * ((float(acc) * input_scale) * weight_scales[col]) + beta * C),
+ * C NULL or c_kind 1 (one value), 2 ([n], per column) or 3 ([m, n]);
+ * activation 0 none, 1 Relu, 2 Silu (Gelu, 3, returns LEAFQ_ERR_UNSUPPORTED).
+ * A MatMul node is alpha = 1, beta = 0, C = NULL.  workspace: at least
+ * leafq_graph_linear_workspace_bytes(m, k) bytes for the codes; a non-finite
+ * input sets *error_flag (device int32, caller clears it). */
+size_t leafq_graph_linear_workspace_bytes(int64_t m, int64_t k);
+int leafq_graph_linear(void* stream, const float* a, int64_t m, int64_t k, int trans_a, const int8_t* weight,
+                       int64_t n, int trans_b, float input_scale, const float* weight_scales, float alpha,
+                       float beta, const float* c, int c_kind, int activation, float* out, void* workspace,
+                       size_t workspace_bytes, int32_t* error_flag);
 
 /* ------------------------------------------------------------------------
  * Persistent decode step.  The reference's forward loop calls linear() for

@@ -8,10 +8,10 @@ operator interface plus the N-sharded multi-GPU wrapper.
 """
 from ._lib import LeafError, LEAFQ_FLAG_PDL, LEAFQ_FLAG_VNNI_ROUNDING, load
 from .linear import (QuantLinearSet, QuantWeight, Workspace, gemm_i8_per_channel,
-                     graph_quantize, linear, linear_int_q, quantize_act)
+                     graph_linear, graph_quantize, linear, linear_int_q, quantize_act)
 
 __all__ = [
     "LeafError", "LEAFQ_FLAG_PDL", "LEAFQ_FLAG_VNNI_ROUNDING", "load", "QuantLinearSet",
-    "QuantWeight", "Workspace", "gemm_i8_per_channel", "graph_quantize", "linear",
+    "QuantWeight", "Workspace", "gemm_i8_per_channel", "graph_linear", "graph_quantize", "linear",
     "linear_int_q", "quantize_act",
 ]

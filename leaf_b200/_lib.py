@@ -43,6 +43,13 @@ _SIGNATURES = {
     "leafq_linear_int_q": ([_vp, _vp, _vp, _i64, _i64, _vp, _vp, _i64, _int, _i64, _vp, _vp, _vp,
                             _u32], _int),
     "leafq_graph_quantize": ([_vp, _vp, _i64, _f32, _vp, _vp], _int),
+    "leafq_linear_smooth_workspace_bytes": ([_i64, _i64, _int], ctypes.c_size_t),
+    "leafq_scale_columns": ([_vp, _vp, _i64, _i64, _vp, _vp], _int),
+    "leafq_linear_smooth": ([_vp, _vp, _vp, _i64, _i64, _vp, _vp, _i64, _int, _i64, _int, _vp, _vp, _vp,
+                             ctypes.c_size_t, ctypes.c_uint32], _int),
+    "leafq_graph_linear_workspace_bytes": ([_i64, _i64], ctypes.c_size_t),
+    "leafq_graph_linear": ([_vp, _vp, _i64, _i64, _int, _vp, _i64, _int, _f32, _vp, _f32, _f32, _vp, _int,
+                            _int, _vp, _vp, ctypes.c_size_t, _vp], _int),
     "leafq_gemm_i8_per_channel": ([_vp, _vp, _vp, _vp, _f32, _vp, _vp, _i64, _i64, _i64, _int],
                                   _int),
     "leafq_linear_w8a8_static_scratch": ([_vp, _vp, _i64, _i64, _vp, _vp, _i64, _vp, _vp, _u32],

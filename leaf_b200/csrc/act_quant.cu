@@ -9,6 +9,8 @@
 // graph_quantize_kernel: the graph executor's static quantiser
 //   (executor.cpp:220-230): division by the calibrated scale, clamp to
 //   [-127, 127], nearbyint.
+#include <algorithm>
+
 #include "leafq_device.cuh"
 #include "leafq_internal.h"
 
@@ -35,26 +37,41 @@ __device__ __forceinline__ float block_max(float v, float* scratch) {
     return scratch[32];
 }
 
+__device__ __forceinline__ float4 scale4(float4 v, const float* __restrict__ col_scale, int64_t i) {
+    if (!col_scale) return v;
+    const float4 f = __ldg(reinterpret_cast<const float4*>(col_scale) + i);
+    return make_float4(__fmul_rn(v.x, f.x), __fmul_rn(v.y, f.y), __fmul_rn(v.z, f.z), __fmul_rn(v.w, f.w));
+}
+
+// col_scale (may be NULL): the calibrated SmoothQuant factors of the
+// weight's input_scale tensor, x[t][col] * col_scale[col] taken before the
+// quantisation (decoder.cpp:1008-1019; one float rounding, as there).
 __global__ void __launch_bounds__(kQuantThreads) quantize_act_kernel(const float* __restrict__ x,
                                                                       int64_t cols,
                                                                       int8_t* __restrict__ q,
-                                                                      float* __restrict__ scales) {
+                                                                      float* __restrict__ scales,
+                                                                      const float* __restrict__ col_scale) {
     __shared__ float scratch[33];
     grid_dependency_wait();
     grid_launch_dependents();
     const int64_t row = blockIdx.x;
     const float* in = x + row * cols;
     int8_t* out = q + row * cols;
-    const bool vec = (cols % 4 == 0) && ((reinterpret_cast<uintptr_t>(in) & 15u) == 0);
+    const bool vec = (cols % 4 == 0) && ((reinterpret_cast<uintptr_t>(in) & 15u) == 0) &&
+                     ((reinterpret_cast<uintptr_t>(col_scale) & 15u) == 0);
+    auto scalar = [&](int64_t i) {
+        const float v = __ldg(in + i);
+        return col_scale ? __fmul_rn(v, __ldg(col_scale + i)) : v;
+    };
     float m = 0.0f;
     if (vec) {
         const float4* in4 = reinterpret_cast<const float4*>(in);
         for (int64_t i = threadIdx.x; i < cols / 4; i += blockDim.x) {
-            const float4 v = __ldg(in4 + i);
+            const float4 v = scale4(__ldg(in4 + i), col_scale, i);
             m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
         }
     } else {
-        for (int64_t i = threadIdx.x; i < cols; i += blockDim.x) m = fmaxf(m, fabsf(__ldg(in + i)));
+        for (int64_t i = threadIdx.x; i < cols; i += blockDim.x) m = fmaxf(m, fabsf(scalar(i)));
     }
     const float absmax = block_max(m, scratch);
     const float scale = fmaxf(__fdiv_rn(absmax, 127.0f), 1e-12f);
@@ -64,13 +81,13 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_act_kernel(const float
         const float4* in4 = reinterpret_cast<const float4*>(in);
         char4* out4 = reinterpret_cast<char4*>(out);
         for (int64_t i = threadIdx.x; i < cols / 4; i += blockDim.x) {
-            const float4 v = __ldg(in4 + i);
+            const float4 v = scale4(__ldg(in4 + i), col_scale, i);
             out4[i] = make_char4(code_of(v.x, multiplier), code_of(v.y, multiplier),
                                  code_of(v.z, multiplier), code_of(v.w, multiplier));
         }
     } else {
         for (int64_t i = threadIdx.x; i < cols; i += blockDim.x)
-            out[i] = code_of(__ldg(in + i), multiplier);
+            out[i] = code_of(scalar(i), multiplier);
     }
 }
 
@@ -95,10 +112,29 @@ __global__ void graph_quantize_kernel(const float* __restrict__ x, int64_t count
 }  // namespace
 
 int launch_quantize_act(cudaStream_t s, const float* x, int64_t tokens, int64_t cols, int8_t* q,
-                        float* scales, bool pdl) {
+                        float* scales, bool pdl, const float* col_scale) {
     if (tokens == 0) return LEAFQ_OK;
     return launch(quantize_act_kernel, dim3(static_cast<unsigned>(tokens)), dim3(kQuantThreads), 0,
-                  s, pdl, "quantize_act", x, cols, q, scales);
+                  s, pdl, "quantize_act", x, cols, q, scales, col_scale);
+}
+
+namespace {
+__global__ void scale_columns_kernel(const float* __restrict__ x, int64_t tokens, int64_t cols,
+                                     const float* __restrict__ col_scale, float* __restrict__ y) {
+    grid_dependency_wait();
+    grid_launch_dependents();
+    const int64_t n = tokens * cols;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        y[i] = __fmul_rn(x[i], __ldg(col_scale + i % cols));
+}
+}  // namespace
+
+int launch_scale_columns(cudaStream_t s, const float* x, int64_t tokens, int64_t cols, const float* col_scale,
+                         float* y, bool pdl) {
+    if (tokens == 0) return LEAFQ_OK;
+    const int64_t blocks = std::min<int64_t>((tokens * cols + 255) / 256, static_cast<int64_t>(sm_count()) * 8);
+    return launch(scale_columns_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, pdl, "scale_columns",
+                  x, tokens, cols, col_scale, y);
 }
 
 int launch_graph_quantize(cudaStream_t s, const float* x, int64_t count, float scale, int8_t* q,

@@ -288,4 +288,119 @@ int leafq_gemm_i8_per_channel(void* stream, const int8_t* a, const int8_t* b, co
                                       weight_scales, out, m, k, n, activation);
 }
 
+int leafq_scale_columns(void* stream, const float* x, int64_t tokens, int64_t cols, const float* col_scale,
+                        float* y) {
+    clear_error();
+    if (tokens < 0 || cols <= 0 || (tokens > 0 && (!x || !col_scale || !y))) {
+        set_error("leafq_scale_columns: invalid arguments");
+        return LEAFQ_ERR_INVALID;
+    }
+    return launch_scale_columns(static_cast<cudaStream_t>(stream), x, tokens, cols, col_scale, y, false);
+}
+
+size_t leafq_linear_smooth_workspace_bytes(int64_t tokens, int64_t cols, int activation_bits) {
+    if (tokens <= 0 || cols <= 0) return 0;
+    if (activation_bits == 8)
+        return align256(static_cast<size_t>(tokens) * static_cast<size_t>(cols)) +
+               align256(static_cast<size_t>(tokens) * sizeof(float));
+    return align256(static_cast<size_t>(tokens) * static_cast<size_t>(cols) * sizeof(float));
+}
+
+int leafq_linear_smooth(void* stream, const float* x, const float* input_scale, int64_t tokens, int64_t cols,
+                        const void* weight, const float* weight_scales, int64_t rows, int bits, int64_t group,
+                        int activation_bits, const float* bias, float* y, void* workspace,
+                        size_t workspace_bytes, uint32_t flags) {
+    if (!input_scale)
+        return leafq_linear(stream, x, tokens, cols, weight, weight_scales, rows, bits, group, activation_bits,
+                            bias, y, workspace, workspace_bytes, flags);
+    clear_error();
+    int st = check_weight(tokens, cols, rows, bits, group, activation_bits);
+    if (st) return st;
+    if (tokens == 0 || rows == 0) return LEAFQ_OK;
+    if (!x || !weight || !y || (bits != 32 && !weight_scales)) {
+        set_error("leafq_linear_smooth: null pointer");
+        return LEAFQ_ERR_INVALID;
+    }
+    if (activation_bits == 8 && bits == 32) {
+        set_error("W32A8 is not a reference path (FP32 weights always use FP32 activations)");
+        return LEAFQ_ERR_INVALID;
+    }
+    const size_t need = leafq_linear_smooth_workspace_bytes(tokens, cols, activation_bits);
+    if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) {
+        set_error("leafq_linear_smooth: this shape needs " + std::to_string(need) +
+                  " bytes of 256-byte aligned workspace");
+        return LEAFQ_ERR_INVALID;
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const bool pdl = (flags & LEAFQ_FLAG_PDL) != 0;
+    if (activation_bits == 8) {
+        // The scaling runs inside the quantiser; then the integer linear.
+        int8_t* q = static_cast<int8_t*>(workspace);
+        float* sx = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
+                                             align256(static_cast<size_t>(tokens) * cols));
+        st = launch_quantize_act(s, x, tokens, cols, q, sx, pdl, input_scale);
+        if (st) return st;
+        if (tokens > kGemvMaxTokens && gemm_tc_supported(tokens, cols, rows, bits, group, weight))
+            return launch_gemm_tc(s, q, sx, tokens, cols, static_cast<const int8_t*>(weight), weight_scales, rows,
+                                  bias, y, pdl);
+        return launch_linear_int_q(s, q, sx, tokens, cols, weight, weight_scales, rows, bits, group, bias, y,
+                                   nullptr, (flags & LEAFQ_FLAG_VNNI_ROUNDING) == 0, pdl);
+    }
+    float* scaled = static_cast<float*>(workspace);
+    st = launch_scale_columns(s, x, tokens, cols, input_scale, scaled, pdl);
+    if (st) return st;
+    if (gemv_w4a32_fast_supported(tokens, cols, bits, group, weight, weight_scales))
+        return launch_gemv_w4a32_fast(s, scaled, cols, static_cast<const uint8_t*>(weight), weight_scales, rows,
+                                      group, bias, y, pdl);
+    return launch_linear_f32act(s, scaled, tokens, cols, weight, weight_scales, rows, bits, group, bias, y, pdl);
+}
+
+size_t leafq_graph_linear_workspace_bytes(int64_t m, int64_t k) {
+    if (m <= 0 || k <= 0) return 0;
+    return align256(static_cast<size_t>(m) * static_cast<size_t>(k));
+}
+
+int leafq_graph_linear(void* stream, const float* a, int64_t m, int64_t k, int trans_a, const int8_t* weight,
+                       int64_t n, int trans_b, float input_scale, const float* weight_scales, float alpha,
+                       float beta, const float* c, int c_kind, int activation, float* out, void* workspace,
+                       size_t workspace_bytes, int32_t* error_flag) {
+    clear_error();
+    if (m < 0 || k <= 0 || n < 0 || m > 65535LL * 64) {
+        set_error("leafq_graph_linear: invalid dimensions");
+        return LEAFQ_ERR_INVALID;
+    }
+    if (!std::isfinite(input_scale) || !(input_scale > 0.0f)) {
+        set_error("invalid activation scale");  // executor.cpp:221
+        return LEAFQ_ERR_INVALID;
+    }
+    if (c && (c_kind < 1 || c_kind > 3)) {
+        set_error("unsupported INT8 Gemm C broadcast shape");  // executor.cpp:601-603
+        return LEAFQ_ERR_INVALID;
+    }
+    if (activation == 3) {
+        set_error("leafq_graph_linear: the fused Gelu (tanhf) is not implemented on the GPU");
+        return LEAFQ_ERR_UNSUPPORTED;
+    }
+    if (activation < 0 || activation > 2) {
+        set_error("leaf::Executor: unsupported fused activation");  // executor.cpp:241
+        return LEAFQ_ERR_INVALID;
+    }
+    if (k > 2147483647LL / (127 * 127)) {
+        set_error("leafq_graph_linear: k exceeds the exact int32 range");
+        return LEAFQ_ERR_UNSUPPORTED;
+    }
+    if (m == 0 || n == 0) return LEAFQ_OK;
+    if (!a || !weight || !weight_scales || !out) {
+        set_error("leafq_graph_linear: null pointer");
+        return LEAFQ_ERR_INVALID;
+    }
+    if (!workspace || workspace_bytes < leafq_graph_linear_workspace_bytes(m, k)) {
+        set_error("leafq_graph_linear: workspace smaller than leafq_graph_linear_workspace_bytes");
+        return LEAFQ_ERR_INVALID;
+    }
+    return launch_graph_linear(static_cast<cudaStream_t>(stream), a, m, k, trans_a ? 1 : 0, weight, n,
+                               trans_b ? 1 : 0, input_scale, weight_scales, alpha, beta, c, c_kind, activation,
+                               out, static_cast<int8_t*>(workspace), error_flag);
+}
+
 }  // extern "C"

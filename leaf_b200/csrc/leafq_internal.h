@@ -67,7 +67,11 @@ struct PeerStore {
 // ------------------------------------------------------------ launchers
 // Each returns a LEAFQ_* status; arguments are validated by the caller.
 int launch_quantize_act(cudaStream_t s, const float* x, int64_t tokens, int64_t cols, int8_t* q,
-                        float* scales, bool pdl);
+                        float* scales, bool pdl, const float* col_scale = nullptr);
+// y[t][c] = x[t][c] * col_scale[c] (SmoothQuant input scaling for the
+// float-activation path).
+int launch_scale_columns(cudaStream_t s, const float* x, int64_t tokens, int64_t cols, const float* col_scale,
+                         float* y, bool pdl);
 
 // Fused act-quant + per-row W8A8 GEMV for tokens <= 8 (bulk-TMA weights).
 bool gemv_w8a8_supported(int64_t tokens, int64_t cols, int bits, int64_t group,
@@ -104,6 +108,14 @@ int launch_gemm_tc(cudaStream_t s, const int8_t* q, const float* sx, int64_t tok
 // Graph executor kernels.
 int launch_graph_quantize(cudaStream_t s, const float* x, int64_t count, float scale, int8_t* q,
                           int32_t* error_flag);
+// execute_quant_linear (executor.cpp:524-614): static quantisation of a
+// (transposed first when trans_a) into codes [m, k], the per-channel GEMM
+// against weight [k, n] or, with trans_b, [n, k], then alpha / beta * C /
+// activation.
+int launch_graph_linear(cudaStream_t s, const float* a, int64_t m, int64_t k, int trans_a,
+                        const int8_t* weight, int64_t n, int trans_b, float input_scale,
+                        const float* wscales, float alpha, float beta, const float* c, int c_kind,
+                        int activation, float* out, int8_t* codes, int32_t* error_flag);
 int launch_gemm_i8_per_channel(cudaStream_t s, const int8_t* a, const int8_t* b,
                                const float* bias, float input_scale, const float* wscales,
                                float* out, int64_t m, int64_t k, int64_t n, int activation);

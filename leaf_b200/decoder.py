@@ -141,6 +141,15 @@ class Decoder:
             for name in ("q", "k", "v", "o"):
                 if get(p + f"self_attn.{name}_proj.bias") is not None:
                     raise LeafError(_lib.LEAFQ_ERR_UNSUPPORTED, "projection biases are not supported")
+            smoothed = [p + f"self_attn.{n}_proj.input_scale" for n in ("q", "k", "v", "o")] + \
+                       [p + f"mlp.{n}_proj.input_scale" for n in ("gate", "up", "down")]
+            if any(get(n) is not None for n in smoothed):
+                # SmoothQuant factors differ per projection, so q|k|v and
+                # gate|up cannot share one quantisation; their linears run
+                # one by one through leafq_linear_smooth instead.
+                raise LeafError(_lib.LEAFQ_ERR_UNSUPPORTED,
+                                "the GPU decoder does not take SmoothQuant artifacts (input_scale tensors); "
+                                "run their linears with leafq_linear_smooth")
         self.final_norm = f32(art.get("model.norm.weight")) if cfg.final_norm else None
         self.lm_head = weight([art.get("lm_head.weight")])
         d, kv = cfg.head_dim, cfg.kv_heads

@@ -127,12 +127,19 @@ def linear(x: torch.Tensor, weight: QuantWeight, activation_bits: int = 8,
     if x.dtype != torch.float32 or x.dim() != 2 or x.shape[1] != weight.cols:
         raise LeafError(_lib.LEAFQ_ERR_INVALID, "input must be float32 [tokens, cols]")
     tokens = x.shape[0]
-    if weight.input_scale is not None:
-        # decoder.cpp:1008-1019: one IEEE multiply per element.
-        x = (x * weight.input_scale).contiguous()
     if out is None:
         out = torch.empty((tokens, weight.rows), dtype=torch.float32, device=x.device)
     lib = load()
+    if weight.input_scale is not None:
+        # decoder.cpp:1008-1019: x * input_scale (one IEEE multiply per
+        # element), fused into the quantiser.
+        need = lib.leafq_linear_smooth_workspace_bytes(tokens, weight.cols, activation_bits)
+        buf = (workspace or Workspace(x.device)).get(need)
+        check(lib.leafq_linear_smooth(_stream(x.device), x.data_ptr(), weight.input_scale.data_ptr(), tokens,
+                                      weight.cols, weight.data.data_ptr(), _ptr(weight.scales), weight.rows,
+                                      weight.bits, weight.group, activation_bits, _ptr(weight.bias),
+                                      out.data_ptr(), buf.data_ptr(), buf.numel(), flags))
+        return out
     need = lib.leafq_linear_workspace_bytes(tokens, weight.cols, weight.bits, weight.group,
                                             activation_bits)
     ws_ptr, ws_bytes = None, 0
@@ -189,6 +196,68 @@ def gemm_i8_per_channel(a: torch.Tensor, b: torch.Tensor, bias: Optional[torch.T
     check(load().leafq_gemm_i8_per_channel(_stream(a.device), a.data_ptr(), b.data_ptr(), _ptr(bias),
                                            float(input_scale), weight_scales.data_ptr(),
                                            out.data_ptr(), m, k, n, 1 if relu else 0))
+    return out
+
+
+_ACTIVATIONS = {None: 0, "": 0, "Relu": 1, "Silu": 2, "Gelu": 3}
+
+
+def graph_linear(a: torch.Tensor, weight: torch.Tensor, weight_scales: torch.Tensor, input_scale: float,
+                 op_type: str = "Gemm", trans_a: bool = False, trans_b: bool = False, alpha: float = 1.0,
+                 beta: float = 1.0, c: Optional[torch.Tensor] = None, activation: Optional[str] = None):
+    """A quantised Gemm / MatMul node of the graph executor
+    (execute_quant_linear, executor.cpp:524-614) on the GPU.
+
+    a: fp32 input ([..., k]; [k, m] with trans_a, Gemm only); weight: int8
+    initializer [k, n] ([n, k] with trans_b); weight_scales: fp32 [n];
+    c: the Gemm's optional third input (one value, [n] or the output shape).
+    MatMul nodes ignore alpha / beta / C as the reference does.  Raises like
+    the reference on a non-finite input or an unsupported broadcast."""
+    _require_cuda(a, "input")
+    _require_cuda(weight, "weight")
+    gemm = op_type == "Gemm"
+    if not gemm:
+        trans_a = trans_b = False
+        alpha, beta, c = 1.0, 0.0, None
+    if a.dim() < 2:
+        raise LeafError(_lib.LEAFQ_ERR_INVALID, "INT8 linear input must be a matrix or batched matrix")
+    if trans_a and a.dim() != 2:
+        raise LeafError(_lib.LEAFQ_ERR_INVALID, "batched INT8 Gemm transA is unsupported")
+    if weight.dim() != 2 or weight.dtype != torch.int8:
+        raise LeafError(_lib.LEAFQ_ERR_INVALID, "INT8 linear weight must be a rank-2 initializer")
+    m = a.shape[1] if trans_a else a.numel() // a.shape[-1]
+    k = a.shape[0] if trans_a else a.shape[-1]
+    n = weight.shape[0] if trans_b else weight.shape[1]
+    if (weight.shape[1] if trans_b else weight.shape[0]) != k:
+        raise LeafError(_lib.LEAFQ_ERR_INVALID, "INT8 linear K dimensions do not match")
+    if weight_scales.numel() != n:
+        raise LeafError(_lib.LEAFQ_ERR_INVALID, "INT8 weight scales do not match output channels")
+    out_shape = (m, n) if trans_a else tuple(a.shape[:-1]) + (n,)
+    c_kind = 0
+    if c is not None:
+        _require_cuda(c, "C")
+        if c.numel() == 1:
+            c_kind = 1
+        elif c.dim() == 1 and c.shape[0] == n:
+            c_kind = 2
+        elif tuple(c.shape) == out_shape:
+            c_kind = 3
+        else:
+            raise LeafError(_lib.LEAFQ_ERR_INVALID, "unsupported INT8 Gemm C broadcast shape")
+        c = c.to(torch.float32).contiguous()
+    if activation not in _ACTIVATIONS:
+        raise LeafError(_lib.LEAFQ_ERR_INVALID, f"leaf::Executor: unsupported fused activation: {activation}")
+    a = a.to(torch.float32).contiguous()
+    out = torch.empty(out_shape, dtype=torch.float32, device=a.device)
+    lib = load()
+    ws = torch.empty(max(lib.leafq_graph_linear_workspace_bytes(m, k), 1), dtype=torch.uint8, device=a.device)
+    flag = torch.zeros(1, dtype=torch.int32, device=a.device)
+    check(lib.leafq_graph_linear(_stream(a.device), a.data_ptr(), m, k, int(trans_a), weight.data_ptr(), n,
+                                 int(trans_b), float(input_scale), weight_scales.contiguous().data_ptr(),
+                                 float(alpha), float(beta), _ptr(c), c_kind, _ACTIVATIONS[activation],
+                                 out.data_ptr(), ws.data_ptr(), ws.numel(), flag.data_ptr()))
+    if int(flag.item()) != 0:
+        raise LeafError(_lib.LEAFQ_ERR_NONFINITE, "INT8 input contains a non-finite value")
     return out
 
 

@@ -159,8 +159,11 @@ class PeerAllGather:
         _require_cuda(x, "input")
         if x.dtype != torch.float32 or x.dim() != 2 or x.shape[1] != shard.cols:
             raise LeafError(_lib.LEAFQ_ERR_INVALID, "input must be float32 [tokens, cols]")
-        if shard.input_scale is not None:
-            x = (x * shard.input_scale).contiguous()
+        if shard.input_scale is not None:  # decoder.cpp:1008-1019
+            scaled = torch.empty_like(x)
+            check(load().leafq_scale_columns(_stream(x.device), x.contiguous().data_ptr(), x.shape[0], shard.cols,
+                                             shard.input_scale.data_ptr(), scaled.data_ptr()))
+            x = scaled
         tokens = x.shape[0]
         if out is None:
             out = torch.empty((tokens, rows), dtype=torch.float32, device=x.device)

@@ -233,6 +233,54 @@ def gemm_i8_per_channel(a, b, bias, input_scale, weight_scales, relu=False):
     return out
 
 
+def graph_linear(a, weight, weight_scales, input_scale, op_type="Gemm", trans_a=False, trans_b=False,
+                 alpha=1.0, beta=1.0, c=None, activation=None):
+    """execute_quant_linear (engine/src/executor.cpp:524-614) restated: the
+    input transposed first with transA (:549-556), quantize_input (:220-230),
+    the weight transposed to [k, n] with transB (:559-568),
+    gemm_i8_per_channel (:574-576), then per element
+    value = alpha * value; value += beta * C[index]; apply_activation
+    (:593-613, :232-242), each step one float32 rounding."""
+    gemm = op_type == "Gemm"
+    if not gemm:
+        trans_a = trans_b = False
+        alpha, beta, c = 1.0, 0.0, None
+    a = _f32(a)
+    if trans_a:
+        a2 = np.ascontiguousarray(a.T)
+        out_shape = (a2.shape[0], None)
+    else:
+        a2 = a.reshape(-1, a.shape[-1])
+        out_shape = tuple(a.shape[:-1]) + (None,)
+    w = np.asarray(weight, dtype=np.int8)
+    wk = np.ascontiguousarray(w.T) if trans_b else w
+    m, k = a2.shape
+    n = wk.shape[1]
+    out_shape = out_shape[:-1] + (n,)
+    qa = graph_quantize(a2, input_scale).reshape(m, k)
+    v = gemm_i8_per_channel(qa, wk, None, input_scale, weight_scales)
+    f = np.float32
+    v = (f(alpha) * v).astype(np.float32)
+    if c is not None:
+        c = _f32(c)
+        if c.size == 1:
+            cb = np.full((m, n), c.reshape(-1)[0], dtype=np.float32)
+        elif c.ndim == 1 and c.shape[0] == n:
+            cb = np.broadcast_to(c, (m, n))
+        elif tuple(c.shape) == out_shape:
+            cb = c.reshape(m, n)
+        else:
+            raise ValueError("unsupported INT8 Gemm C broadcast shape")
+        v = (v + (f(beta) * cb).astype(np.float32)).astype(np.float32)
+    if activation == "Relu":
+        v = np.where(v < 0, f(0), v).astype(np.float32)
+    elif activation == "Silu":
+        v = (v / (f(1) + expf(-v))).astype(np.float32)
+    elif activation not in (None, ""):
+        raise ValueError(f"activation {activation} not restated")
+    return v.reshape(out_shape)
+
+
 # --------------------------------------------------------------------------
 # the reference's own kernels (oracle/_ref)
 # --------------------------------------------------------------------------

@@ -270,3 +270,24 @@ def test_streams_are_independent(cuda_device):
     torch.cuda.synchronize()
     for x, y in zip(xs, outs):
         assert bits_equal(y.cpu().numpy(), oracle.linear_int(x, payload, scales, 8, 2048, None))
+
+
+@pytest.mark.parametrize("m", [1, 5, 40])
+@pytest.mark.parametrize("bits,group,abits", [(8, 512, 8), (8, 64, 8), (4, 32, 8), (4, 32, 32), (8, 512, 32)])
+def test_smoothquant_input_scale(cuda_device, m, bits, group, abits):
+    """A weight with a calibrated input_scale (decoder.cpp:1008-1019): the
+    input times the factors (one float rounding) is what the linear sees;
+    leafq_linear_smooth fuses the scaling into the quantiser."""
+    rng = np.random.default_rng(m * 100 + bits + group + abits)
+    k, n = 512, 96
+    payload, scales = make_weight(rng, n, k, bits, group)
+    x = activations(rng, m, k)
+    factors = (rng.random(k) * 1.5 + 0.5).astype(np.float32)
+    w = lq.QuantWeight.from_host(payload, scales, n, k, bits, group, None, factors)
+    y = host(lq.linear(dev(x), w, abits))
+    xs = (x * factors[None, :]).astype(np.float32)
+    if abits == 8:
+        expect = oracle.linear_int(xs, payload, scales, bits, group, None)
+    else:
+        expect = oracle.linear_float(xs, payload, scales, bits, group, None)
+    assert bits_equal(y, expect)
