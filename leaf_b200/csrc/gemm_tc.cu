@@ -14,8 +14,9 @@
 // chunks, batched decode of a few dozen sequences, where the weight stream
 // is the cost and must come through all SMs), else 32.  Operands are K-major: the
 // codes [tokens, cols] and the weights [rows, cols] are both row-major with
-// K contiguous, loaded by TMA with 128-byte swizzle into a 4-stage ring
-// (48 KB per stage).  Warp roles (192 threads, persistent over tiles):
+// K contiguous, loaded by TMA with 128-byte swizzle into a ring of 4 to 10
+// stages (about 200 KB); with at most 64 tokens the code box is cut to 32 or
+// 64 rows.  Warp roles (192 threads, persistent over tiles):
 //   warp 0: TMA producer (one elected lane), no multicast;
 //   warp 1: allocates 512 TMEM columns (two 256-column accumulators so the
 //           epilogue of one tile overlaps the MMAs of the next) and issues
@@ -39,14 +40,23 @@ constexpr int UMMA_K = 32;
 constexpr int kThreads = 192;
 constexpr int kABytes = BM * BK;  // 16 KB
 
-template <int BN>
+// kThin (at most 64 tokens, one M tile): each stage holds only 64 rows of
+// codes, so twice as many stages fit and a whole K of 2048 is in flight at
+// once.  The MMA still reads 128 rows; rows 64..127 fall on the next
+// stage's bytes (or the weight tiles after the last stage) -- in bounds,
+// and their accumulator lanes are never stored.
+template <int BN, bool kThin>
 struct TileCfg {
+    static constexpr int kAStage = kThin ? 64 * BK : kABytes;
+    static constexpr int kBBytes = BN * BK;
     // As many 128-byte K stages as fit in ~200 KB of shared memory.
-    static constexpr int kStages = BN == 256 ? 4 : BN == 128 ? 6 : BN == 64 ? 8 : 10;
+    static constexpr int kStages = kThin ? (196608 / (kAStage + kBBytes) < 16 ? 196608 / (kAStage + kBBytes) : 16)
+                                         : (BN == 256 ? 4 : BN == 128 ? 6 : BN == 64 ? 8 : 10);
     static constexpr int kAccCols = BN;  // TMEM columns per accumulator
     static constexpr int kTmemCols = 2 * kAccCols;
-    static constexpr int kBBytes = BN * BK;
-    static constexpr size_t kSmemBytes = (size_t)kStages * (kABytes + kBBytes) + 1024 /*barriers*/ + 1024 /*align*/;
+    static constexpr size_t kSmemBytes = (size_t)kStages * (kAStage + kBBytes) + 1024 /*barriers*/ + 1024 /*align*/;
+    static_assert(!kThin || (size_t)kStages * kBBytes >= (size_t)(kABytes - kAStage),
+                  "the last thin stage's unused rows must stay inside the tile region");
 };
 
 struct GemmArgs {
@@ -59,16 +69,19 @@ struct GemmArgs {
     int64_t cols;
     int m_tiles;
     int n_tiles;
+    uint32_t a_box_bytes;  // bytes one A load brings (box rows x 128): fewer rows for few tokens
 };
 
-template <int BN>
+template <int BN, bool kThin>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_w8a8_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_w,
                     const GemmArgs a) {
-    constexpr int kStages = TileCfg<BN>::kStages;
-    constexpr int kAccCols = TileCfg<BN>::kAccCols;
-    constexpr int kTmemCols = TileCfg<BN>::kTmemCols;
-    constexpr int kBBytes = TileCfg<BN>::kBBytes;
+    using Cfg = TileCfg<BN, kThin>;
+    constexpr int kStages = Cfg::kStages;
+    constexpr int kAccCols = Cfg::kAccCols;
+    constexpr int kTmemCols = Cfg::kTmemCols;
+    constexpr int kBBytes = Cfg::kBBytes;
+    constexpr int kABytes = Cfg::kAStage;  // bytes of one stage's code tile
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte alignment for the swizzled operand tiles.
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -119,7 +132,7 @@ gemm_w8a8_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
             {
                 const int n0 = (blockIdx.x / a.m_tiles) * BN;
                 for (int kb = 0; kb < early; ++kb) {
-                    mbar_arrive_expect_tx(&full[kb], kABytes + kBBytes);
+                    mbar_arrive_expect_tx(&full[kb], a.a_box_bytes + kBBytes);
                     tma_load_2d(b_tiles + (size_t)kb * kBBytes, &map_w, kb * BK, n0, &full[kb], keep);
                 }
             }
@@ -139,7 +152,7 @@ gemm_w8a8_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&full[s], kABytes + kBBytes);
+                    mbar_arrive_expect_tx(&full[s], a.a_box_bytes + kBBytes);
                     tma_load_2d(a_tiles + (size_t)s * kABytes, &map_q, kb * BK, m0, &full[s], keep);
                     tma_load_2d(b_tiles + (size_t)s * kBBytes, &map_w, kb * BK, n0, &full[s], keep);
                 }
@@ -287,21 +300,26 @@ bool gemm_tc_supported(int64_t tokens, int64_t cols, int64_t rows, int bits, int
 }
 
 namespace {
-template <int BN>
+template <int BN, bool kThin>
 int run_tiles(cudaStream_t s, const int8_t* q, const int8_t* weight, int64_t cols, int64_t tokens,
               int64_t rows, GemmArgs a, bool pdl) {
     CUtensorMap map_q, map_w;
-    int st = make_map(&map_q, q, cols, tokens, BM);
+    // With one M tile of few tokens the A box is cut to 32 or 64 rows: the
+    // tile's other rows are never stored (their accumulator lanes are
+    // dropped by the epilogue), so loading them would only cost bandwidth.
+    const int a_rows = kThin ? (tokens <= 32 ? 32 : 64) : BM;
+    a.a_box_bytes = static_cast<uint32_t>(a_rows * BK);
+    int st = make_map(&map_q, q, cols, tokens, a_rows);
     if (st) return st;
     st = make_map(&map_w, weight, cols, rows, BN);
     if (st) return st;
     a.n_tiles = static_cast<int>((rows + BN - 1) / BN);
     const int64_t tiles = (int64_t)a.m_tiles * a.n_tiles;
     const int grid = static_cast<int>(std::min<int64_t>(tiles, sm_count()));
-    constexpr size_t smem = TileCfg<BN>::kSmemBytes;
-    st = allow_smem(reinterpret_cast<const void*>(gemm_w8a8_tc_kernel<BN>), smem, "gemm_w8a8_tc");
+    constexpr size_t smem = TileCfg<BN, kThin>::kSmemBytes;
+    st = allow_smem(reinterpret_cast<const void*>(gemm_w8a8_tc_kernel<BN, kThin>), smem, "gemm_w8a8_tc");
     if (st) return st;
-    return launch(gemm_w8a8_tc_kernel<BN>, dim3(grid), dim3(kThreads), smem, s, pdl, "gemm_w8a8_tc",
+    return launch(gemm_w8a8_tc_kernel<BN, kThin>, dim3(grid), dim3(kThreads), smem, s, pdl, "gemm_w8a8_tc",
                   map_q, map_w, a);
 }
 }  // namespace
@@ -321,10 +339,16 @@ int launch_gemm_tc(cudaStream_t s, const int8_t* q, const float* sx, int64_t tok
     a.cols = cols;
     a.m_tiles = static_cast<int>((tokens + BM - 1) / BM);
     auto tiles = [&](int64_t bn) { return (int64_t)a.m_tiles * ((rows + bn - 1) / bn); };
-    if (tiles(256) >= sm_count()) return run_tiles<256>(s, q, weight, cols, tokens, rows, a, pdl);
-    if (tiles(128) >= sm_count()) return run_tiles<128>(s, q, weight, cols, tokens, rows, a, pdl);
-    if (tiles(64) >= sm_count()) return run_tiles<64>(s, q, weight, cols, tokens, rows, a, pdl);
-    return run_tiles<32>(s, q, weight, cols, tokens, rows, a, pdl);
+    if (tokens <= 64) {
+        if (tiles(256) >= sm_count()) return run_tiles<256, true>(s, q, weight, cols, tokens, rows, a, pdl);
+        if (tiles(128) >= sm_count()) return run_tiles<128, true>(s, q, weight, cols, tokens, rows, a, pdl);
+        if (tiles(64) >= sm_count()) return run_tiles<64, true>(s, q, weight, cols, tokens, rows, a, pdl);
+        return run_tiles<32, true>(s, q, weight, cols, tokens, rows, a, pdl);
+    }
+    if (tiles(256) >= sm_count()) return run_tiles<256, false>(s, q, weight, cols, tokens, rows, a, pdl);
+    if (tiles(128) >= sm_count()) return run_tiles<128, false>(s, q, weight, cols, tokens, rows, a, pdl);
+    if (tiles(64) >= sm_count()) return run_tiles<64, false>(s, q, weight, cols, tokens, rows, a, pdl);
+    return run_tiles<32, false>(s, q, weight, cols, tokens, rows, a, pdl);
 }
 
 }  // namespace leafq

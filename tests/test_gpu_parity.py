@@ -172,11 +172,11 @@ def test_w8a8_prefill_gemm_down_proj(cuda_device):
 
 
 @pytest.mark.parametrize("m,k,n", [(9, 1040, 300), (200, 2064, 257), (129, 128, 513), (640, 512, 256),
-                                   (16, 256, 9500), (64, 2048, 2560), (64, 512, 20000)])
+                                   (16, 256, 9500), (64, 2048, 2560), (64, 512, 20000), (40, 256, 38000)])
 def test_w8a8_prefill_gemm_ragged(cuda_device, m, k, n):
     """Tiles cut by M, N and K edges (K a multiple of 16 but not of 128), and
-    every tile width (on 148 SMs: 32, 64, 128 and 256 rows per tile for the
-    last three shapes and the decode-batch shapes)."""
+    every tile width (on 148 SMs: 32, 64, 128 and 256 rows per tile), with
+    the thin code tiles of launches of at most 64 tokens."""
     rng = np.random.default_rng(m + k + n)
     payload, scales = make_weight(rng, n, k, 8, k)
     x = activations(rng, m, k)
