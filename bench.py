@@ -87,6 +87,8 @@ CASES = {
     "w4": (1, 11008, 4096, 4, 32, 32),          # config 1 INT4 weight-only GEMV
     "decode_small": None,                        # persistent decode kernel, 3-layer stack
     "model_small": None,                         # whole-model decode kernel, 3-layer model
+    "batch_step": None,                          # config 4: 64 x 512 prefill + 2 decode steps, 22 layers
+    "batch_step_small": None,                    # the same with 2 layers (for --set full captures)
 }
 
 
@@ -114,6 +116,28 @@ def run_case(name):
             raise RuntimeError("device status not ok")
         print(json.dumps({"case": name, "layers": 3, "status": "ok"}))
         dec.close()
+        return
+    if name in ("batch_step", "batch_step_small"):
+        # Config 4's operators: a 64 x 512-token batched prefill, then two
+        # decode steps of all 64 sequences (per-operator launches, no graph,
+        # so every kernel appears in a launch list).
+        from leaf_b200.decoder import Decoder
+        from leaf_b200.stack import RandomDecoderModel, StackShape
+
+        torch.cuda.set_device(0)
+        layers = 22 if name == "batch_step" else 2
+        model = RandomDecoderModel(StackShape(layers=layers), seed=1)
+        dec = Decoder(model, sequences=BATCH_SEQUENCES, capacity=BATCH_PROMPT + 8)
+        model.release()
+        prompts = np.random.default_rng(0).integers(0, 32000, size=(BATCH_SEQUENCES, BATCH_PROMPT)).tolist()
+        dec.forward_batch(prompts)
+        b = dec._bufs(1)
+        for _ in range(2):
+            dec._forward_device(b, 1)
+        torch.cuda.synchronize()
+        if dec.device_status() != 0:
+            raise RuntimeError("device status not ok")
+        print(json.dumps({"case": name, "layers": layers, "sequences": BATCH_SEQUENCES, "status": "ok"}))
         return
     if name == "decode_small":
         # The persistent decode kernel on a 3-layer TinyLlama-width stack

@@ -9,10 +9,10 @@
 //   y = fma(float(acc) * sx[token], sw[row], 0.0f) + (bias[row] or 0.0f).
 //
 // Tiling: D[128 tokens, BN rows] per tile (one UMMA of M=128, N=BN, K=32
-// per instruction, four per 128-byte K block); BN = 256, or the widest of
-// 128 / 64 / 32 whose tiles still give every SM one (few tokens: prefill
-// chunks, batched decode of a few dozen sequences, where the weight stream
-// is the cost and must come through all SMs), else 32.  Operands are K-major: the
+// per instruction, four per 128-byte K block); BN = 256 or 128 when their
+// tiles give every SM one, else 64 when its tiles cover about 4/5 of the
+// SMs, else 32 (few tokens: prefill chunks, batched decode of a few dozen
+// sequences, where the weight stream must come through most SMs).  Operands are K-major: the
 // codes [tokens, cols] and the weights [rows, cols] are both row-major with
 // K contiguous, loaded by TMA with 128-byte swizzle into a ring of 4 to 10
 // stages (about 200 KB); with at most 64 tokens the code box is cut to 32 or
@@ -338,16 +338,21 @@ int launch_gemm_tc(cudaStream_t s, const int8_t* q, const float* sx, int64_t tok
     a.rows = rows;
     a.cols = cols;
     a.m_tiles = static_cast<int>((tokens + BM - 1) / BM);
+    // 256- or 128-row tiles when they give every SM one; 64-row tiles when
+    // they cover about 4/5 of the SMs (measured: one wave of those beats two
+    // waves of 32-row tiles, while wide tiles short of one per SM lose to
+    // narrower ones); else 32.
+    const int64_t sms = sm_count();
     auto tiles = [&](int64_t bn) { return (int64_t)a.m_tiles * ((rows + bn - 1) / bn); };
     if (tokens <= 64) {
-        if (tiles(256) >= sm_count()) return run_tiles<256, true>(s, q, weight, cols, tokens, rows, a, pdl);
-        if (tiles(128) >= sm_count()) return run_tiles<128, true>(s, q, weight, cols, tokens, rows, a, pdl);
-        if (tiles(64) >= sm_count()) return run_tiles<64, true>(s, q, weight, cols, tokens, rows, a, pdl);
+        if (tiles(256) >= sms) return run_tiles<256, true>(s, q, weight, cols, tokens, rows, a, pdl);
+        if (tiles(128) >= sms) return run_tiles<128, true>(s, q, weight, cols, tokens, rows, a, pdl);
+        if (tiles(64) * 5 >= sms * 4) return run_tiles<64, true>(s, q, weight, cols, tokens, rows, a, pdl);
         return run_tiles<32, true>(s, q, weight, cols, tokens, rows, a, pdl);
     }
-    if (tiles(256) >= sm_count()) return run_tiles<256, false>(s, q, weight, cols, tokens, rows, a, pdl);
-    if (tiles(128) >= sm_count()) return run_tiles<128, false>(s, q, weight, cols, tokens, rows, a, pdl);
-    if (tiles(64) >= sm_count()) return run_tiles<64, false>(s, q, weight, cols, tokens, rows, a, pdl);
+    if (tiles(256) >= sms) return run_tiles<256, false>(s, q, weight, cols, tokens, rows, a, pdl);
+    if (tiles(128) >= sms) return run_tiles<128, false>(s, q, weight, cols, tokens, rows, a, pdl);
+    if (tiles(64) * 5 >= sms * 4) return run_tiles<64, false>(s, q, weight, cols, tokens, rows, a, pdl);
     return run_tiles<32, false>(s, q, weight, cols, tokens, rows, a, pdl);
 }
 
