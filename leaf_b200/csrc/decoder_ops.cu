@@ -344,7 +344,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
 }
 
 // attention_group_kernel: the decode form.  Block (t, kv head, s) serves
-// the `group` query heads that share one kv head, so each key and value row
+// the query heads that share one kv head (all of them, or half when the
+// grid would be small: head_split), so each key and value row
 // is staged in shared memory once for all of them (coalesced loads; the next
 // chunk is loaded into registers while the current one is used).
 //   dots:  thread (h, k) of a chunk of min(64, kGroupThreads / group) keys,
@@ -374,7 +375,7 @@ __global__ void __launch_bounds__(kGroupThreads) attention_group_kernel(
     const float* __restrict__ q_heads, const float* __restrict__ k_cache,
     const float* __restrict__ v_cache, int64_t tokens, int heads, int kv_heads,
     const int32_t* __restrict__ positions, int64_t capacity, float scale, float* __restrict__ out,
-    const __grid_constant__ ExpTable tab_g) {
+    int head_split, const __grid_constant__ ExpTable tab_g) {
     // The table in shared memory: lanes index it with different k, which the
     // constant bank would serialise.
     __shared__ ExpTable tab;
@@ -388,10 +389,13 @@ __global__ void __launch_bounds__(kGroupThreads) attention_group_kernel(
     __shared__ __align__(16) float rows_s[kGroupRows * kLd];
     __shared__ float red[kGroupThreads / 32];
     __shared__ float max_s[kGroupMaxHeads], den_s[kGroupMaxHeads];
-    const int group = heads / kv_heads;
+    // head_split blocks share one kv head, each serving `group` of its
+    // query heads (more blocks in flight when sequences x kv heads is small).
+    const int group = heads / kv_heads / head_split;
     const int chunk = min(kGroupRows, kGroupThreads / group);  // 32 or 64 keys
-    const int64_t t = blockIdx.x;
+    const int64_t t = blockIdx.x / head_split;
     const int kvh = blockIdx.y;
+    const int head0 = kvh * group * head_split + static_cast<int>(blockIdx.x % head_split) * group;
     const int64_t seq = blockIdx.z;
     const int64_t start = positions[seq];
     if (start < 0 || start + tokens > capacity) {
@@ -414,7 +418,7 @@ __global__ void __launch_bounds__(kGroupThreads) attention_group_kernel(
     }
     for (int i = tid; i < group * DIM; i += kGroupThreads) {
         const int h = i / DIM, d = i % DIM;
-        q_s[i] = q_heads[((seq * heads + kvh * group + h) * tokens + t) * DIM + d];
+        q_s[i] = q_heads[((seq * heads + head0 + h) * tokens + t) * DIM + d];
     }
     // ---- dots
     const int my_h = tid / chunk, my_k = tid % chunk;
@@ -518,7 +522,7 @@ __global__ void __launch_bounds__(kGroupThreads) attention_group_kernel(
 #pragma unroll
     for (int j = 0; j < kAcc; ++j) {
         const int h = h0 + j * kPass;
-        if (h < group) out[((seq * tokens + t) * heads + kvh * group + h) * (int64_t)DIM + d] = acc[j];
+        if (h < group) out[((seq * tokens + t) * heads + head0 + h) * (int64_t)DIM + d] = acc[j];
     }
 }
 
@@ -956,19 +960,24 @@ int leafq_attention_batch(void* stream, const float* q_heads, const float* k_cac
     const size_t group_smem = static_cast<size_t>(group) * ld * sizeof(float);
     if ((dim == 32 || dim == 64) && group <= kGroupMaxHeads && aligned16(k_cache) && aligned16(v_cache) &&
         group_smem + 24 * 1024 <= static_cast<size_t>(max_smem_per_block())) {
-        const dim3 grid(static_cast<unsigned>(tokens), kv_heads, static_cast<unsigned>(sequences));
+        // Two blocks per kv head (each with half of its query heads) when one
+        // per kv head would leave most SMs idle (measured: a gain for 8
+        // sequences, a loss for 64).
+        const int head_split =
+            (group % 2 == 0 && 2 * tokens * kv_heads * sequences <= static_cast<int64_t>(sm_count())) ? 2 : 1;
+        const dim3 grid(static_cast<unsigned>(tokens * head_split), kv_heads, static_cast<unsigned>(sequences));
         if (dim == 32) {
             int st = allow_smem(reinterpret_cast<const void*>(attention_group_kernel<32>), group_smem, "attention");
             if (st) return st;
             return launch(attention_group_kernel<32>, grid, dim3(kGroupThreads), group_smem, s, false,
                           "attention", q_heads, k_cache, v_cache, tokens, heads, kv_heads, positions, capacity,
-                          scale, out, exp_table());
+                          scale, out, head_split, exp_table());
         }
         int st = allow_smem(reinterpret_cast<const void*>(attention_group_kernel<64>), group_smem, "attention");
         if (st) return st;
         return launch(attention_group_kernel<64>, grid, dim3(kGroupThreads), group_smem, s, false, "attention",
                       q_heads, k_cache, v_cache, tokens, heads, kv_heads, positions, capacity, scale, out,
-                      exp_table());
+                      head_split, exp_table());
     }
     const size_t smem = (static_cast<size_t>(dim) + capacity) * sizeof(float);
     if (smem > static_cast<size_t>(max_smem_per_block())) {

@@ -54,7 +54,9 @@ struct TileCfg {
                                          : (BN == 256 ? 4 : BN == 128 ? 6 : BN == 64 ? 8 : 10);
     static constexpr int kAccCols = BN;  // TMEM columns per accumulator
     static constexpr int kTmemCols = 2 * kAccCols;
-    static constexpr size_t kSmemBytes = (size_t)kStages * (kAStage + kBBytes) + 1024 /*barriers*/ + 1024 /*align*/;
+    static constexpr size_t kColBytes = 4 * 2 * 2 * BN * sizeof(float);  // [warp][acc][scale | bias][BN]
+    static constexpr size_t kSmemBytes =
+        (size_t)kStages * (kAStage + kBBytes) + 1024 /*barriers*/ + kColBytes + 1024 /*align*/;
     static_assert(!kThin || (size_t)kStages * kBBytes >= (size_t)(kABytes - kAStage),
                   "the last thin stage's unused rows must stay inside the tile region");
 };
@@ -93,6 +95,9 @@ gemm_w8a8_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
     uint64_t* acc_full = empty + kStages;
     uint64_t* acc_empty = acc_full + 2;
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acc_empty + 2);
+    // Each tile's row scales and bias, staged per tile by every epilogue
+    // warp for itself (two copies: one per accumulator).
+    float* col_s = reinterpret_cast<float*>(b_tiles + (size_t)kStages * kBBytes + 1024);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int kblocks = static_cast<int>((a.cols + BK - 1) / BK);
@@ -203,6 +208,17 @@ gemm_w8a8_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
             const int acc = local & 1;
             const int m0 = (tile % a.m_tiles) * BM;
             const int n0 = (tile / a.m_tiles) * BN;
+            // Stage this tile's row scales and bias (0 without bias: the
+            // epilogue always adds it) while the MMAs run; this warp's own
+            // copy, so no other warp is waited on.
+            float* ws_s = col_s + (quarter * 2 + acc) * 2 * BN;
+            float* bias_s = ws_s + BN;
+            for (int i = lane; i < BN; i += 32) {
+                const int64_t n = n0 + i < a.rows ? n0 + i : a.rows - 1;
+                ws_s[i] = __ldg(a.ws + n);
+                bias_s[i] = a.bias ? __ldg(a.bias + n) : 0.0f;
+            }
+            __syncwarp();
             if (!mbar_wait(&acc_full[acc], (local >> 1) & 1, kSiteGemmAccFull)) break;
             tcgen05_fence_after();
             const int64_t m = m0 + quarter * 32 + lane;
@@ -218,12 +234,15 @@ gemm_w8a8_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
                 if (!row_live || nb >= a.rows) continue;
                 float v[32];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int64_t n = nb + j;
-                    const int64_t nn = n < a.rows ? n : a.rows - 1;
-                    const float product = __fmul_rn(__int2float_rn(static_cast<int>(r[j])), token_scale);
-                    const float result = __fmaf_rn(product, __ldg(a.ws + nn), 0.0f);
-                    v[j] = __fadd_rn(result, a.bias ? __ldg(a.bias + nn) : 0.0f);
+                for (int j = 0; j < 32; j += 4) {
+                    const float4 w4 = *reinterpret_cast<const float4*>(ws_s + c + j);
+                    const float4 b4 = *reinterpret_cast<const float4*>(bias_s + c + j);
+                    const float wv[4] = {w4.x, w4.y, w4.z, w4.w}, bv[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const float product = __fmul_rn(__int2float_rn(static_cast<int>(r[j + u])), token_scale);
+                        v[j + u] = __fadd_rn(__fmaf_rn(product, wv[u], 0.0f), bv[u]);
+                    }
                 }
                 if (vec && nb + 32 <= a.rows) {
 #pragma unroll
