@@ -382,6 +382,12 @@ int leafq_attention_batch(void* stream, const float* q_heads, const float* k_cac
  * ..., the output of one linear over interleaved gate / up rows) -> out
  * [tokens][width] = u * (g / (1 + expf(-g))) (decoder.cpp:982-988, 1414). */
 int leafq_silu_gate(void* stream, const float* gate_up, int64_t tokens, int64_t width, float* out);
+/* leafq_silu_gate with the per-token INT8 quantisation of the result fused
+ * in: codes [tokens][width] and scales [tokens] exactly as
+ * leafq_quantize_act quantises the activations (the input of the down
+ * projection, for leafq_linear_int_q); act may be NULL.  width <= 6144. */
+int leafq_silu_gate_quantize(void* stream, const float* gate_up, int64_t tokens, int64_t width, float* act,
+                             int8_t* codes, float* code_scales);
 /* ids[r] = first index of the largest value of logits row r
  * (std::max_element, main_decoder.cpp:101). */
 int leafq_argmax(void* stream, const float* logits, int64_t rows, int64_t width, int32_t* ids);

@@ -79,6 +79,7 @@ _SIGNATURES = {
     "leafq_attention_batch": ([_vp, _vp, _vp, _vp, _int, _i64, _int, _int, _int, _vp, _i64, _i64, _f32, _vp,
                                _vp, _i64], _int),
     "leafq_silu_gate": ([_vp, _vp, _i64, _i64, _vp], _int),
+    "leafq_silu_gate_quantize": ([_vp, _vp, _i64, _i64, _vp, _vp, _vp], _int),
     "leafq_argmax": ([_vp, _vp, _i64, _i64, _vp], _int),
     "leafq_expf": ([_vp, _vp, _i64, _vp], _int),
     "leafq_advance_position": ([_vp, _vp, ctypes.c_int32], _int),

@@ -715,6 +715,46 @@ __global__ void silu_gate_kernel(const float* __restrict__ gate_up, int64_t toke
     }
 }
 
+// The SiLU gate with the per-token INT8 quantisation of the down
+// projection's input fused in: block t computes row t's activations (kept in
+// registers, up to kSiluQuantPer per thread), their absmax, and the codes and
+// scale leafq_quantize_act would produce from them.  act (may be NULL) also
+// receives the fp32 activations.
+constexpr int kSiluQuantThreads = 512;
+constexpr int kSiluQuantPer = 12;  // width <= 512 * 12 = 6144
+
+__global__ void __launch_bounds__(kSiluQuantThreads) silu_gate_quantize_kernel(
+    const float* __restrict__ gate_up, int64_t width, float* __restrict__ act, int8_t* __restrict__ codes,
+    float* __restrict__ code_scales, const __grid_constant__ ExpTable tab_g) {
+    __shared__ ExpTable tab;
+    if (threadIdx.x < 32) tab.bits[threadIdx.x] = tab_g.bits[threadIdx.x];
+    __shared__ float scratch[33];
+    __syncthreads();
+    const int64_t t = blockIdx.x;
+    const float2* gu = reinterpret_cast<const float2*>(gate_up) + t * width;
+    float v[kSiluQuantPer];
+    float m = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kSiluQuantPer; ++j) {
+        const int64_t c = threadIdx.x + (int64_t)j * kSiluQuantThreads;
+        if (c < width) {
+            const float2 p = __ldg(gu + c);
+            v[j] = silu_gate_one(p.x, p.y, tab);
+            if (act) act[t * width + c] = v[j];
+            m = fmaxf(m, fabsf(v[j]));
+        }
+    }
+    const float absmax = block_max(m, scratch);
+    const float scale = fmaxf(__fdiv_rn(absmax, 127.0f), 1e-12f);
+    const float multiplier = __fdiv_rn(1.0f, scale);
+    if (threadIdx.x == 0) code_scales[t] = scale;
+#pragma unroll
+    for (int j = 0; j < kSiluQuantPer; ++j) {
+        const int64_t c = threadIdx.x + (int64_t)j * kSiluQuantThreads;
+        if (c < width) codes[t * width + c] = act_code(v[j], multiplier);
+    }
+}
+
 // ----------------------------------------------------------------- argmax
 __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* __restrict__ logits,
                                                                  int64_t width,
@@ -1036,6 +1076,23 @@ int leafq_silu_gate(void* stream, const float* gate_up, int64_t tokens, int64_t 
     const int64_t blocks = std::min<int64_t>((items + 255) / 256, static_cast<int64_t>(sm_count()) * 8);
     return launch(silu_gate_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0,
                   static_cast<cudaStream_t>(stream), false, "silu_gate", gate_up, tokens, width, out, vec,
+                  exp_table());
+}
+
+int leafq_silu_gate_quantize(void* stream, const float* gate_up, int64_t tokens, int64_t width, float* act,
+                             int8_t* codes, float* code_scales) {
+    clear_error();
+    if (tokens < 0 || tokens > 0x7fffffff || width <= 0 || width > kSiluQuantThreads * kSiluQuantPer) {
+        set_error("leafq_silu_gate_quantize: width must be 1..6144");
+        return LEAFQ_ERR_INVALID;
+    }
+    if (tokens == 0) return LEAFQ_OK;
+    if (!gate_up || !codes || !code_scales) {
+        set_error("leafq_silu_gate_quantize: null pointer");
+        return LEAFQ_ERR_INVALID;
+    }
+    return launch(silu_gate_quantize_kernel, dim3(static_cast<unsigned>(tokens)), dim3(kSiluQuantThreads), 0,
+                  static_cast<cudaStream_t>(stream), false, "silu_gate", gate_up, width, act, codes, code_scales,
                   exp_table());
 }
 

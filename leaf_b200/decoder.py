@@ -196,6 +196,7 @@ class Decoder:
                      down=e(rows, c.hidden), last=e(S, c.hidden), logits=e(S, c.vocab),
                      workspace=Workspace(dev),
                      codes=torch.empty((rows, c.hidden), dtype=torch.int8, device=dev),
+                     codes_mlp=torch.empty((rows, c.intermediate), dtype=torch.int8, device=dev),
                      code_scales=e(rows))
             # Each chunk size owns its workspace, sized once: a captured graph
             # keeps its pointers, so nothing it uses may be reallocated.
@@ -332,9 +333,21 @@ class Decoder:
             self._linear(b["attn"], layer["o"], b["o"], rows, b["workspace"])
             norm(b["o"], 0, layer["post_norm"], fuse)
             normed_linear(layer["gate_up"], b["gate_up"])
-            check(lib.leafq_silu_gate(s, b["gate_up"].data_ptr(), rows, c.intermediate,
-                                      b["act"].data_ptr()))
-            self._linear(b["act"], layer["down"], b["down"], rows, b["workspace"])
+            if fuse and c.intermediate <= 6144:
+                # SiLU gate and the down projection's quantisation in one pass.
+                check(lib.leafq_silu_gate_quantize(s, b["gate_up"].data_ptr(), rows, c.intermediate, None,
+                                                   b["codes_mlp"].data_ptr(), b["code_scales"].data_ptr()))
+                w = layer["down"]
+                dst, gather = self._sharded_out(w, b["down"], rows)
+                check(lib.leafq_linear_int_q(s, b["codes_mlp"].data_ptr(), b["code_scales"].data_ptr(), rows,
+                                             w.cols, w.data.data_ptr(), w.scales.data_ptr(), w.rows, w.bits,
+                                             w.group, None, dst.data_ptr(), None, LEAFQ_FLAG_PDL))
+                if gather is not None:
+                    gather()
+            else:
+                check(lib.leafq_silu_gate(s, b["gate_up"].data_ptr(), rows, c.intermediate,
+                                          b["act"].data_ptr()))
+                self._linear(b["act"], layer["down"], b["down"], rows, b["workspace"])
             last = i + 1 == len(self.layers)
             if last and self.final_norm is None:
                 # no final norm: the logits would read the residual stream itself

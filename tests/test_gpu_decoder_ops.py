@@ -123,3 +123,13 @@ def test_rotary_attention_silu_bit_exact(cuda_device):
     g, u = gu[:, 0::2], gu[:, 1::2]
     expect = u * (g / (np.float32(1) + oracle.expf(-g)))
     assert np.array_equal(act.cpu().numpy().view(np.uint32), expect.view(np.uint32))
+    # The same gate with the down projection's INT8 quantisation fused in.
+    act2 = torch.empty((3, 1000), device="cuda")
+    codes = torch.empty((3, 1000), dtype=torch.int8, device="cuda")
+    sx = torch.empty(3, device="cuda")
+    lq._lib.check(lib.leafq_silu_gate_quantize(_s(), torch.from_numpy(gu).cuda().data_ptr(), 3, 1000,
+                                               act2.data_ptr(), codes.data_ptr(), sx.data_ptr()))
+    eq, esx = oracle.quantize_act(expect)
+    assert np.array_equal(act2.cpu().numpy().view(np.uint32), expect.view(np.uint32))
+    assert np.array_equal(codes.cpu().numpy(), eq)
+    assert np.array_equal(sx.cpu().numpy().view(np.uint32), esx.view(np.uint32))
