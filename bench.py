@@ -56,6 +56,9 @@ def parse():
                    help="batch workload on N GPUs: dp = the sequences split over the ranks (full "
                         "weights each); tp = every linear's rows split over the ranks with an NCCL "
                         "all-gather of each output (all sequences on every rank)")
+    p.add_argument("--tp-gather", choices=("peer", "nccl"), default="peer",
+                   help="tp decode-step gathers: the library's peer-memory all-gather over NVLink "
+                        "(captured in the step's CUDA graph) or NCCL (eager)")
     p.add_argument("--case", choices=sorted(CASES),
                    help="run one small single-kernel case three times and exit (for ncu captures)")
     return p.parse_args()
@@ -504,7 +507,7 @@ def run_batch(args, rank, world, local_rank):
     shape = StackShape()
     model = RandomDecoderModel(shape, seed=1234, device=device)
     dec = Decoder(model, device=device, sequences=seqs, capacity=BATCH_PROMPT + BATCH_GENERATED,
-                  group=dist.group.WORLD if tp else None)
+                  group=dist.group.WORLD if tp else None, gather=args.tp_gather)
     model.release()
     del model
     lib = lq.load()
@@ -572,6 +575,7 @@ def run_batch(args, rank, world, local_rank):
     if status != 0:
         raise RuntimeError(f"device status {status}: {lib.leafq_last_error().decode()}")
     assert all(len(t) == steps + 1 for t in tokens)
+    dec.close()
 
     value = BATCH_SEQUENCES * steps / (decode_ms * 1e-3)
     if rank == 0:
@@ -604,8 +608,9 @@ def run_batch(args, rank, world, local_rank):
                             f"positions {BATCH_PROMPT}..{BATCH_PROMPT + steps - 1}",
                 "model": "TinyLlama-1.1B shape (random-init INT8 per-row weights)",
                 "global_batch": BATCH_SEQUENCES, "seq_len": BATCH_PROMPT + BATCH_GENERATED,
-                "parallelism": (f"tp{world} (every linear's rows split over the GPUs, NCCL all-gather of "
-                                f"each output; all {seqs} sequences on every GPU)") if tp else
+                "parallelism": (f"tp{world} (every linear's rows split over the GPUs, each output "
+                                f"all-gathered: decode steps by {args.tp_gather}, the prompt by NCCL; all "
+                                f"{seqs} sequences on every GPU)") if tp else
                                f"dp{world} ({seqs} sequences per GPU, full weights each)",
                 "l2": "inputs larger than L2 (1.04 GB of weights and the KV caches streamed per step)",
             },

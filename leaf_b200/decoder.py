@@ -67,7 +67,8 @@ def _concat_rows(parts: list[HostTensor], device: torch.device, interleave: bool
 
 class Decoder:
     def __init__(self, artifact, activation_bits: int = 8, device="cuda",
-                 capacity: Optional[int] = None, sequences: int = 1, group=None):
+                 capacity: Optional[int] = None, sequences: int = 1, group=None,
+                 gather: str = "nccl"):
         """artifact: a path, an ``Artifact``, or any object with the same
         ``config`` / ``get(name)`` interface whose payloads are tensors
         (``leaf_b200.stack.RandomDecoderModel``).
@@ -85,7 +86,10 @@ class Decoder:
         and the slices are all-gathered (NCCL) into the full output on every
         rank; the other operators run on every rank.  Rows are independent,
         so the results are the unsharded ones bit for bit.  Every rank must
-        make the same calls."""
+        make the same calls.  gather="peer" gathers the decode steps' outputs
+        with the library's own peer-memory all-gather over NVLink
+        (``leafq_allgather_*``), which lets the step be one CUDA graph; the
+        prompt's gathers stay NCCL."""
         art = artifact if hasattr(artifact, "get") else Artifact(artifact)
         cfg = art.config
         if not (cfg.norm_kind == 0 and cfg.position_kind == 0 and cfg.gated == 1 and
@@ -108,6 +112,10 @@ class Decoder:
             self.world, self.rank = 1, 0
         self._full_rows: dict[int, int] = {}
         self._gather_bufs: dict = {}
+        if gather not in ("nccl", "peer"):
+            raise LeafError(_lib.LEAFQ_ERR_INVALID, "gather must be 'nccl' or 'peer'")
+        self._peer = None
+        self._peer_kind = gather if self.world > 1 else "nccl"
         self.activation_bits = activation_bits
         self.device = torch.device(device)
         self.capacity = int(capacity or cfg.max_positions)
@@ -250,6 +258,11 @@ class Decoder:
         def gather():
             import torch.distributed as dist
 
+            if self._peer is not None and tokens == self.sequences:
+                # Decode step: this rank's rows stored into every rank's
+                # buffer over NVLink, collected in row order (graph-capturable).
+                self._peer.run(local, self.rank * n, self.world * n, out)
+                return
             if tokens == 1:  # [world][n] is already the row order of [1, world * n]
                 dist.all_gather_into_tensor(out.view(-1), local.view(-1), group=self.group)
             else:
@@ -403,10 +416,15 @@ class Decoder:
         """Capture one decode step (ids from the previous step's argmax) as
         a CUDA graph.  A sharded decoder steps without a graph (its NCCL
         gathers run eagerly)."""
-        if self.world > 1:
+        if self.world > 1 and self._peer_kind == "nccl":
             self._bufs(1)
             self._step_ready = True
             return
+        if self.world > 1 and self._peer is None:
+            from .parallel import PeerAllGather
+
+            widest = max(self._full_rows.values())
+            self._peer = PeerAllGather(self.sequences * widest, group=self.group)
         b = self._bufs(1)
         stream = torch.cuda.Stream(self.device)
         stream.wait_stream(torch.cuda.current_stream(self.device))
@@ -565,6 +583,10 @@ class Decoder:
         return out
 
     def close(self) -> None:
+        if self._peer is not None:
+            self.graph = None  # the graph holds the peer kernels
+            self._peer.close()
+            self._peer = None
         if self._plan is not None:
             torch.cuda.synchronize(self.device)
             check(self.lib.leafq_model_plan_destroy(self._plan))

@@ -135,10 +135,13 @@ def _decoder_rank_main(rank, world, port, path, prompts, new_tokens, failures, r
                             timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
     try:
-        dec = Decoder(path, sequences=len(prompts), group=dist.group.WORLD)
-        got = dec.generate_batch(prompts, new_tokens)
-        if dec.device_status() != 0:
-            failures.put(f"rank {rank}: device status")
+        got = {}
+        for gather in ("nccl", "peer"):
+            dec = Decoder(path, sequences=len(prompts), group=dist.group.WORLD, gather=gather)
+            got[gather] = dec.generate_batch(prompts, new_tokens)
+            if dec.device_status() != 0:
+                failures.put(f"rank {rank} {gather}: device status")
+            dec.close()
         results.put((rank, got))
     except Exception as exc:  # noqa: BLE001
         failures.put(f"rank {rank}: {exc!r}")
@@ -147,9 +150,10 @@ def _decoder_rank_main(rank, world, port, path, prompts, new_tokens, failures, r
 
 
 def test_sharded_decoder_two_gpus(tmp_path):
-    """The batched decoder with every linear's rows split over 2 GPUs (NCCL
-    all-gather of each output): every sequence's tokens equal the unsharded
-    decoder's, and the first is the reference's recorded request."""
+    """The batched decoder with every linear's rows split over 2 GPUs (each
+    output all-gathered by NCCL, or in the decode steps by the peer-memory
+    gather inside the step's CUDA graph): every sequence's tokens equal the
+    unsharded decoder's, and the first is the reference's recorded request."""
     if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import decoder_fixture as fx  # tests/golden
@@ -188,4 +192,5 @@ def test_sharded_decoder_two_gpus(tmp_path):
         errors.append(failures.get())
     assert not errors, errors
     assert not alive, "a rank did not finish"
-    assert got.get(0) == expect and got.get(1) == expect
+    for rank in (0, 1):
+        assert got.get(rank) == {"nccl": expect, "peer": expect}, rank
