@@ -531,6 +531,17 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
         }
         const int64_t vecs = op.cols / 4;
         float4 xr[kXVec];
+        // The norm's weights do not depend on x: requested before waiting for
+        // it, so the normalisation after the in-order sum finds them loaded.
+        float4 nw[kXVec];
+        if (op.xsrc != kXTagged) {
+#pragma unroll
+            for (int k = 0; k < kXVec; ++k) {
+                const int64_t i = tid + (int64_t)k * kNC;
+                nw[k] = i < vecs ? __ldg(reinterpret_cast<const float4*>(op.norm_w) + i)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
         if (op.xsrc == kXTagged) {
             if (ok && !load_tagged_x(op.x_ll, vecs, tag, tid, xr)) {
                 ok = false;
@@ -571,7 +582,7 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
             for (int k = 0; k < kXVec; ++k) {
                 const int64_t i = tid + (int64_t)k * kNC;
                 if (i < vecs) {
-                    const float4 w = __ldg(reinterpret_cast<const float4*>(op.norm_w) + i);
+                    const float4 w = nw[k];
                     float4 v = xr[k];
                     v.x = __fadd_rn(__fmul_rn(__fmul_rn(v.x, scale), w.x), 0.0f);
                     v.y = __fadd_rn(__fmul_rn(__fmul_rn(v.y, scale), w.y), 0.0f);
@@ -583,12 +594,15 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
         }
         // Residual inputs of this warp's rows, one lane per row block (the
         // hidden vector is complete: this op's input was derived from it).
-        float row_resid = 0.0f;
+        // The word is requested now and its tag checked after the
+        // quantisation, so the load's latency hides behind it.
+        int64_t resid_r = -1;
+        uint64_t resid_word = 0;
         if (op.epi == kEpiResidTagged && rows_in_regs && ok && group + 2 * lane < g.nblocks) {
             const int64_t r = g.row0 + (int64_t)(group + 2 * lane) * kRowsPerStage + wi;
-            if (r < g.row1 && !wait_tagged(op.resid_ll + r, tag, row_resid)) {
-                ok = false;
-                *abort_flag = 1;
+            if (r < g.row1) {
+                resid_r = r;
+                resid_word = load_tagged(op.resid_ll + r);
             }
         }
         // Per-token INT8 quantisation of x (decoder.cpp:1028-1038).
@@ -615,6 +629,15 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
                                      to_code(xr[k].w, mul));
         }
         consumer_sync();
+        float row_resid = 0.0f;
+        if (resid_r >= 0) {
+            if (static_cast<uint32_t>(resid_word >> 32) == tag) {
+                row_resid = __uint_as_float(static_cast<uint32_t>(resid_word));
+            } else if (ok && !wait_tagged(op.resid_ll + resid_r, tag, row_resid)) {
+                ok = false;
+                *abort_flag = 1;
+            }
+        }
         const int cols = static_cast<int>(op.cols);
         float best = -INFINITY;
         int32_t best_r = 0x7fffffff;
