@@ -143,7 +143,8 @@ __device__ __forceinline__ void load_tagged2(const uint64_t* p, uint64_t& a, uin
 
 // x[4i .. 4i+3] for this thread's kXVec float4s, as tagged words: the
 // loads of two float4s are issued together, then their tags are checked (a
-// word not yet written is polled, bounded).  Returns false if a wait gave up.
+// float4 with a word not yet written is polled as a whole, bounded).
+// Returns false if a wait gave up.
 __device__ __forceinline__ bool load_tagged_x(const uint64_t* x, int64_t vecs, uint32_t tag, int tid,
                                               float4 (&xr)[kXVec]) {
     bool good = true;
@@ -163,17 +164,33 @@ __device__ __forceinline__ bool load_tagged_x(const uint64_t* x, int64_t vecs, u
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
             const int64_t i = tid + (int64_t)(k0 + k) * kNC;
-            float v[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                if (static_cast<uint32_t>(w[k][e] >> 32) == tag) {
-                    v[e] = __uint_as_float(static_cast<uint32_t>(w[k][e]));
-                } else if (!(good && wait_tagged(x + 4 * i + e, tag, v[e]))) {
-                    good = false;
-                    v[e] = 0.0f;
+            auto all_tagged = [&]() {
+                return static_cast<uint32_t>(w[k][0] >> 32) == tag && static_cast<uint32_t>(w[k][1] >> 32) == tag &&
+                       static_cast<uint32_t>(w[k][2] >> 32) == tag && static_cast<uint32_t>(w[k][3] >> 32) == tag;
+            };
+            if (i < vecs && good && !all_tagged()) {
+                // Not all four written yet: poll the four words together (one
+                // round trip per poll; they come from neighbouring rows, so
+                // they land together), bounded.
+                const unsigned long long start = global_timer_ns();
+                for (uint32_t spins = 1;; ++spins) {
+                    load_tagged2(x + 4 * i, w[k][0], w[k][1]);
+                    load_tagged2(x + 4 * i + 2, w[k][2], w[k][3]);
+                    if (all_tagged()) break;
+                    if ((spins & 31u) == 0u &&
+                        (device_error_raised() || global_timer_ns() - start > kWaitLimitNs)) {
+                        record_device_error(kSiteDecodeDependency);
+                        good = false;
+                        break;
+                    }
                 }
             }
-            xr[k0 + k] = i < vecs ? make_float4(v[0], v[1], v[2], v[3]) : make_float4(0.f, 0.f, 0.f, 0.f);
+            xr[k0 + k] = i < vecs && good
+                             ? make_float4(__uint_as_float(static_cast<uint32_t>(w[k][0])),
+                                           __uint_as_float(static_cast<uint32_t>(w[k][1])),
+                                           __uint_as_float(static_cast<uint32_t>(w[k][2])),
+                                           __uint_as_float(static_cast<uint32_t>(w[k][3])))
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
         }
     }
     return good;
@@ -383,6 +400,12 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
                 issue(kc, kbuf, &att_bar[0], 0);
                 issue(vc, vbuf, &att_bar[1], 0);
             }
+            // This position's rotation (independent of q and k), before the wait.
+            float rope_c = 0.0f, rope_s = 0.0f;
+            if (tid < half) {
+                rope_c = m.cos_table[pos * half + tid];
+                rope_s = m.sin_table[pos * half + tid];
+            }
             for (int i = tid; i < 3 * dim; i += kNC) {
                 const int part = i / dim, d = i % dim;
                 const int64_t src = part == 0 ? (int64_t)head * dim + d
@@ -398,7 +421,7 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
             consumer_sync();
             // RoPE on q and k (decoder.cpp:1271-1279), in place.
             if (tid < half) {
-                const float c = m.cos_table[pos * half + tid], sn = m.sin_table[pos * half + tid];
+                const float c = rope_c, sn = rope_s;
                 const float a = qs[tid], b = qs[tid + half];
                 const float ka = ks[tid], kb = ks[tid + half];
                 qs[tid] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, sn));
