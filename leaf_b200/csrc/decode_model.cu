@@ -56,6 +56,7 @@ constexpr int kStageBarriers = 16;
 constexpr int kMaxCols = 8192;
 constexpr int kXVec = kMaxCols / 4 / kNC;
 constexpr int kScratchFloats = 4096;  // hidden row for RMSNorm; attention scores + V chunk
+constexpr int kNormXVec = kScratchFloats / 4 / kNC;  // float4s of a normalised (hidden) row per thread
 constexpr int kMaxCapacity = 2048;    // attention scores (first half of the scratch)
 constexpr int kMaxDim = 256;
 constexpr int kAttFloats = static_cast<int>((kRingBytes - kAttnRingBytes) / 4) + kMaxCols / 4 + kScratchFloats;
@@ -96,7 +97,8 @@ struct Model {
 
 constexpr size_t kSmemBytes = (size_t)kRingBytes + kMaxCols + kScratchFloats * 4 + 3 * kMaxDim * 4 +
                               2 * (kStageBarriers + 2) * 8 + kStageBarriers * 8 + 2 * 2 * 8 * 4 +
-                              kConsumerWarps * 12 + 64 + sizeof(ExpTable) + 8;
+                              kConsumerWarps * 12 + 64 + sizeof(ExpTable) + 8 +
+                              sizeof(OrderedSumScratch<kNC>) + 16;
 
 __device__ __forceinline__ void consumer_sync() {
     asm volatile("bar.sync 1, %0;" ::"n"(kNC) : "memory");
@@ -290,6 +292,8 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
     // expf's table in shared memory (lanes index it with different k, which
     // the constant bank would serialise).
     ExpTable* tab_s = reinterpret_cast<ExpTable*>((reinterpret_cast<uintptr_t>(total_s + 2) + 7) & ~uintptr_t(7));
+    OrderedSumScratch<kNC>* sum_ws =
+        reinterpret_cast<OrderedSumScratch<kNC>*>((reinterpret_cast<uintptr_t>(tab_s + 1) + 15) & ~uintptr_t(15));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tid = threadIdx.x;
@@ -556,10 +560,10 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
         float4 xr[kXVec];
         // The norm's weights do not depend on x: requested before waiting for
         // it, so the normalisation after the in-order sum finds them loaded.
-        float4 nw[kXVec];
+        float4 nw[kNormXVec];
         if (op.xsrc != kXTagged) {
 #pragma unroll
-            for (int k = 0; k < kXVec; ++k) {
+            for (int k = 0; k < kNormXVec; ++k) {
                 const int64_t i = tid + (int64_t)k * kNC;
                 nw[k] = i < vecs ? __ldg(reinterpret_cast<const float4*>(op.norm_w) + i)
                                  : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -584,25 +588,38 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
                 ok = false;
                 *abort_flag = 1;
             }
-            // Squares in parallel; then one thread adds them left to right
-            // (the additions are the only dependent chain).
+            // Squares in parallel; then their left-to-right sum, bit for bit:
+            // by all consumer threads (sum_in_order_par) for rows of up to
+            // 4 * kNC values, else by one thread.
             float* sq4 = scratch;
+            float4 sq0 = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-            for (int k = 0; k < kXVec; ++k) {
+            for (int k = 0; k < kNormXVec; ++k) {
                 const int64_t i = tid + (int64_t)k * kNC;
-                if (i < vecs)
-                    reinterpret_cast<float4*>(sq4)[i] =
-                        make_float4(__fmul_rn(xr[k].x, xr[k].x), __fmul_rn(xr[k].y, xr[k].y),
-                                    __fmul_rn(xr[k].z, xr[k].z), __fmul_rn(xr[k].w, xr[k].w));
+                if (i < vecs) {
+                    const float4 q = make_float4(__fmul_rn(xr[k].x, xr[k].x), __fmul_rn(xr[k].y, xr[k].y),
+                                                 __fmul_rn(xr[k].z, xr[k].z), __fmul_rn(xr[k].w, xr[k].w));
+                    reinterpret_cast<float4*>(sq4)[i] = q;
+                    if (k == 0) sq0 = q;
+                }
             }
             consumer_sync();
             if (*abort_flag) return;
-            if (tid == 0) *total_s = sum_in_order(sq4, static_cast<int>(op.cols));
-            consumer_sync();
+            float sumsq;
+            if (op.cols <= 4 * kNC) {
+                sumsq = sum_in_order_par<kNC>(sq0, sq4, static_cast<int>(op.cols), tid, *sum_ws,
+                                              [] { consumer_sync(); });
+            } else {
+                if (tid == 0) *total_s = sum_in_order(sq4, static_cast<int>(op.cols));
+                consumer_sync();
+                sumsq = *total_s;
+            }
             const float scale =
-                __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(*total_s, static_cast<float>(op.cols)), m.epsilon)));
+                __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sumsq, static_cast<float>(op.cols)), m.epsilon)));
 #pragma unroll
-            for (int k = 0; k < kXVec; ++k) {
+            for (int k = kNormXVec; k < kXVec; ++k) xr[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int k = 0; k < kNormXVec; ++k) {
                 const int64_t i = tid + (int64_t)k * kNC;
                 if (i < vecs) {
                     const float4 w = nw[k];

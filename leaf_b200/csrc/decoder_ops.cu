@@ -103,7 +103,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(
     const float* __restrict__ weight, float epsilon, float* __restrict__ out) {
     extern __shared__ float row[];  // [width] values, then [width] squares
     float* squares = row + width;
-    __shared__ float total;
+    __shared__ float sequential_total;  // the sum of squares
     const int64_t t = blockIdx.x;
     float* h = hidden + t * width;
     for (int64_t c = threadIdx.x; c < width; c += blockDim.x) {
@@ -120,34 +120,38 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(
     __syncthreads();
     if (threadIdx.x == 0) {
         if ((width & 3) == 0) {
-            total = sum_in_order(squares, static_cast<int>(width));
+            sequential_total = sum_in_order(squares, static_cast<int>(width));
         } else {
             float sq = 0.0f;
             for (int64_t c = 0; c < width; ++c) sq = __fadd_rn(sq, squares[c]);
-            total = sq;
+            sequential_total = sq;
         }
     }
     __syncthreads();
+    const float total = sequential_total;
     const float scale =
         __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(width)), epsilon)));
     for (int64_t c = threadIdx.x; c < width; c += blockDim.x)
         out[t * width + c] = __fadd_rn(__fmul_rn(__fmul_rn(row[c], scale), weight[c]), 0.0f);
 }
 
-// The same operator for rows of width % 4 == 0, width <= 4 * 4 * kNormThreads,
-// 16-byte aligned: each thread keeps its (up to 16) values in registers, so
-// the row is read once with all loads in flight.  Optionally the normalised
-// row is quantised to per-token INT8 codes in the same pass (the quantiser
-// of leafq_quantize_act, bit for bit), for a W8A8 linear that follows.
-constexpr int kNormVec = 4;
+// The same operator for rows of width % 4 == 0, width <= 4 * 2 * kNormVecThreads,
+// 16-byte aligned: each thread keeps its (up to 8) values in registers, so
+// the row is read once with all loads in flight; rows of up to 2048 values
+// sum their squares with the whole block (sum_in_order_par).  Optionally the
+// normalised row is quantised to per-token INT8 codes in the same pass (the
+// quantiser of leafq_quantize_act, bit for bit), for a W8A8 linear that
+// follows.
+constexpr int kNormVec = 2;
+constexpr int kNormVecThreads = 512;
 
-__global__ void __launch_bounds__(kNormThreads) rmsnorm_vec_kernel(
+__global__ void __launch_bounds__(kNormVecThreads) rmsnorm_vec_kernel(
     float* __restrict__ hidden, const float* __restrict__ delta, int add_zero, int64_t width,
     const float* __restrict__ weight, float epsilon, float* __restrict__ out, int8_t* __restrict__ codes,
     float* __restrict__ code_scales) {
     extern __shared__ __align__(16) float squares[];  // [width]
-    __shared__ float total;
     __shared__ float scratch[33];
+    __shared__ OrderedSumScratch<kNormVecThreads> sum_ws;
     const int64_t t = blockIdx.x;
     const int n4 = static_cast<int>(width / 4);
     float4* h4 = reinterpret_cast<float4*>(hidden + t * width);
@@ -156,7 +160,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_vec_kernel(
     float4 v[kNormVec], w[kNormVec], dv[kNormVec];
 #pragma unroll
     for (int j = 0; j < kNormVec; ++j) {
-        const int c = threadIdx.x + j * kNormThreads;
+        const int c = threadIdx.x + j * kNormVecThreads;
         if (c < n4) {
             v[j] = h4[c];
             if (d4) dv[j] = __ldg(d4 + c);
@@ -165,7 +169,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_vec_kernel(
     }
 #pragma unroll
     for (int j = 0; j < kNormVec; ++j) {
-        const int c = threadIdx.x + j * kNormThreads;
+        const int c = threadIdx.x + j * kNormVecThreads;
         if (c < n4) {
             if (d4) {
                 float4 d = dv[j];
@@ -181,15 +185,24 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_vec_kernel(
         }
     }
     __syncthreads();
-    if (threadIdx.x == 0) total = sum_in_order(squares, static_cast<int>(width));
-    __syncthreads();
+    float total;
+    if (width <= 4 * kNormVecThreads) {
+        const float4 sq0 = threadIdx.x < n4 ? reinterpret_cast<const float4*>(squares)[threadIdx.x]
+                                            : make_float4(0.f, 0.f, 0.f, 0.f);
+        total = sum_in_order_par<kNormVecThreads>(sq0, squares, static_cast<int>(width), threadIdx.x, sum_ws,
+                                                  [] { __syncthreads(); });
+    } else {
+        if (threadIdx.x == 0) scratch[32] = sum_in_order(squares, static_cast<int>(width));
+        __syncthreads();
+        total = scratch[32];
+    }
     const float scale =
         __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(width)), epsilon)));
     float4 o[kNormVec];
     float absmax = 0.0f;
 #pragma unroll
     for (int j = 0; j < kNormVec; ++j) {
-        const int c = threadIdx.x + j * kNormThreads;
+        const int c = threadIdx.x + j * kNormVecThreads;
         if (c < n4) {
             o[j] = make_float4(__fadd_rn(__fmul_rn(__fmul_rn(v[j].x, scale), w[j].x), 0.0f),
                                __fadd_rn(__fmul_rn(__fmul_rn(v[j].y, scale), w[j].y), 0.0f),
@@ -207,7 +220,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_vec_kernel(
     char4* c4 = reinterpret_cast<char4*>(codes + t * width);
 #pragma unroll
     for (int j = 0; j < kNormVec; ++j) {
-        const int c = threadIdx.x + j * kNormThreads;
+        const int c = threadIdx.x + j * kNormVecThreads;
         if (c < n4)
             c4[c] = make_char4(act_code(o[j].x, multiplier), act_code(o[j].y, multiplier),
                                act_code(o[j].z, multiplier), act_code(o[j].w, multiplier));
@@ -854,14 +867,14 @@ int leafq_rmsnorm_quantize(void* stream, float* hidden, const float* delta, int 
         return LEAFQ_ERR_INVALID;
     }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const bool vec = width % 4 == 0 && width <= 4 * kNormVec * kNormThreads && aligned16(hidden) &&
+    const bool vec = width % 4 == 0 && width <= 4 * kNormVec * kNormVecThreads && aligned16(hidden) &&
                      (!delta || aligned16(delta)) && aligned16(weight) && (!out || aligned16(out)) &&
                      (!codes || reinterpret_cast<uintptr_t>(codes) % 4 == 0);
     const size_t smem = static_cast<size_t>(width) * sizeof(float);
     if (vec) {
         int st = allow_smem(reinterpret_cast<const void*>(rmsnorm_vec_kernel), smem, "rmsnorm");
         if (st) return st;
-        return launch(rmsnorm_vec_kernel, dim3(static_cast<unsigned>(tokens)), dim3(kNormThreads), smem, s, false,
+        return launch(rmsnorm_vec_kernel, dim3(static_cast<unsigned>(tokens)), dim3(kNormVecThreads), smem, s, false,
                       "rmsnorm", hidden, delta, add_zero, width, weight, epsilon, out, codes, code_scales);
     }
     if (codes) {

@@ -38,25 +38,33 @@ def _vectors(rng, kind, rows, width):
         return (g * np.float32(1e18)).astype(np.float32)
     if kind == "pow2":
         return np.ldexp(np.float32(1), rng.integers(-10, 10, size=g.shape)).astype(np.float32)
+    if kind == "ones":  # partial sums land exactly on powers of two
+        return np.sign(g).astype(np.float32)
+    if kind == "growing":  # the running sum changes binade at almost every element
+        e = (np.arange(width) % 48) - 40
+        return (np.ldexp(np.float32(1), e)[None, :] * (1 + np.abs(g) * 0.01)).astype(np.float32)
     raise ValueError(kind)
 
 
-@pytest.mark.parametrize("width", [64, 100, 102, 2048, 3000])
-@pytest.mark.parametrize("kind", ["normal", "outliers", "grid", "zeros", "tiny", "huge", "pow2"])
+@pytest.mark.parametrize("width", [64, 100, 102, 2048, 3000, 4096])
+@pytest.mark.parametrize("kind", ["normal", "outliers", "grid", "zeros", "tiny", "huge", "pow2", "ones", "growing"])
 def test_rmsnorm_bit_exact(cuda_device, kind, width):
     rng = np.random.default_rng(hash((kind, width)) % 2**32)
-    rows = 48
+    rows = 512 if kind == "normal" and width == 2048 else 48
     x = _vectors(rng, kind, rows, width)
     delta = rng.standard_normal((rows, width)).astype(np.float32)
     w = (1 + 0.1 * rng.standard_normal(width)).astype(np.float32)
-    for add_zero in (0, 1):
+    # No residual first (the built inputs reach the norm as they are), then
+    # with the residual added, with and without the "+ 0.0f" of the delta.
+    for use_delta, add_zero in ((False, 0), (True, 0), (True, 1)):
         h = torch.from_numpy(x).cuda()
         d = torch.from_numpy(delta).cuda()
+        d_ptr = d.data_ptr() if use_delta else None
         out = torch.empty_like(h)
-        lq._lib.check(lq.load().leafq_rmsnorm(_s(), h.data_ptr(), d.data_ptr(), add_zero, rows, width,
+        lq._lib.check(lq.load().leafq_rmsnorm(_s(), h.data_ptr(), d_ptr, add_zero, rows, width,
                                               torch.from_numpy(w).cuda().data_ptr(), ctypes.c_float(1e-5),
                                               out.data_ptr()))
-        hx = x + ((delta + np.float32(0)) if add_zero else delta)
+        hx = x + ((delta + np.float32(0)) if add_zero else delta) if use_delta else x
         assert np.array_equal(h.cpu().numpy().view(np.uint32), hx.view(np.uint32))
         with np.errstate(over="ignore", invalid="ignore"):
             expect = od.rmsnorm(hx, w, 1e-5)
@@ -68,7 +76,7 @@ def test_rmsnorm_bit_exact(cuda_device, kind, width):
             codes = torch.empty((rows, width), dtype=torch.int8, device="cuda")
             sx = torch.empty(rows, device="cuda")
             lq._lib.check(lq.load().leafq_rmsnorm_quantize(
-                _s(), h.data_ptr(), d.data_ptr(), add_zero, rows, width, torch.from_numpy(w).cuda().data_ptr(),
+                _s(), h.data_ptr(), d_ptr, add_zero, rows, width, torch.from_numpy(w).cuda().data_ptr(),
                 ctypes.c_float(1e-5), None, codes.data_ptr(), sx.data_ptr()))
             eq, esx = oracle.quantize_act(expect)
             assert np.array_equal(codes.cpu().numpy(), eq), kind
