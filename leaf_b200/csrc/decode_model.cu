@@ -45,7 +45,9 @@ namespace leafq {
 namespace {
 
 constexpr int kConsumerWarps = 16;
-constexpr int kRowsPerStage = 8;  // = warps per consumer group
+constexpr int kRowsPerStage = 8;  // rows per ring stage (one bulk copy)
+constexpr int kGroups = 4;        // consumer warp groups: group q takes the stages rb % kGroups == q
+constexpr int kGroupWarps = 4;    // warps per group, two rows of a stage each
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kNC = kConsumerWarps * 32;  // consumer threads
 constexpr uint32_t kRingBytes = 192 * 1024;
@@ -102,10 +104,6 @@ constexpr size_t kSmemBytes = (size_t)kRingBytes + kMaxCols + kScratchFloats * 4
 
 __device__ __forceinline__ void consumer_sync() {
     asm volatile("bar.sync 1, %0;" ::"n"(kNC) : "memory");
-}
-
-__device__ __forceinline__ void group_sync(int group) {
-    asm volatile("bar.sync %0, %1;" ::"r"(2 + group), "n"(kRowsPerStage * 32) : "memory");
 }
 
 __device__ __forceinline__ uint64_t load_tagged(const uint64_t* p) {
@@ -229,18 +227,20 @@ __device__ __forceinline__ int block_rows(const OpGeometry& g, int rb) {
     return static_cast<int>(min64(kRowsPerStage, g.row1 - g.row0 - (int64_t)rb * kRowsPerStage));
 }
 
-// Row scale (and the residual input, for residual epilogues) of row block
-// (group + 2 * lane), row wi, of `op`, in lane `lane` of the warp: lane k
-// holds the values the warp needs for its k-th row block, so the epilogue
-// never waits on a load.  Zero beyond 64 row blocks (the epilogue then loads
-// directly).
-__device__ __forceinline__ float load_row_scale(const MOp& op, const OpGeometry& g, int group, int wi,
-                                                int lane) {
-    if (g.nblocks <= 2 * 32 && group + 2 * lane < g.nblocks) {
-        const int64_t r = g.row0 + (int64_t)(group + 2 * lane) * kRowsPerStage + wi;
-        if (r < g.row1) return __ldg(op.ws + r);
+// Row scales (and the residual inputs, for residual epilogues) of rows
+// 2 wi and 2 wi + 1 of row block (group + kGroups * lane) of `op`, in lane
+// `lane` of the warp: lane k holds the values the warp needs for its k-th
+// row block, so the epilogue never waits on a load.  Zero beyond
+// 32 * kGroups row blocks (the epilogue then loads directly).
+__device__ __forceinline__ float2 load_row_scales(const MOp& op, const OpGeometry& g, int group, int wi,
+                                                  int lane) {
+    float2 r = make_float2(0.0f, 0.0f);
+    if (g.nblocks <= kGroups * 32 && group + kGroups * lane < g.nblocks) {
+        const int64_t r0 = g.row0 + (int64_t)(group + kGroups * lane) * kRowsPerStage + 2 * wi;
+        if (r0 < g.row1) r.x = __ldg(op.ws + r0);
+        if (r0 + 1 < g.row1) r.y = __ldg(op.ws + r0 + 1);
     }
-    return 0.0f;
+    return r;
 }
 
 struct RingCursor {
@@ -283,8 +283,7 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
     uint64_t* att_bar = full + kStageBarriers;  // [2] attention K / V staging
     uint64_t* empty = att_bar + 2;
     uint64_t* stage_end = empty + kStageBarriers;
-    float* pair_y = reinterpret_cast<float*>(stage_end + kStageBarriers);  // [2 buf][2 group][8]
-    float* partial_max = pair_y + 32;                                   // [kConsumerWarps]
+    float* partial_max = reinterpret_cast<float*>(stage_end + kStageBarriers) + 32;  // [kConsumerWarps]
     float* best_v = partial_max + kConsumerWarps;                       // [kConsumerWarps]
     int32_t* best_row = reinterpret_cast<int32_t*>(best_v + kConsumerWarps);
     float* total_s = reinterpret_cast<float*>(best_row + kConsumerWarps);
@@ -300,7 +299,7 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
     if (tid == 0) {
         for (int b = 0; b < kStageBarriers; ++b) {
             mbar_init(&full[b], 1);
-            mbar_init(&empty[b], kRowsPerStage);
+            mbar_init(&empty[b], kGroupWarps);
         }
         mbar_init(&att_bar[0], 1);
         mbar_init(&att_bar[1], 1);
@@ -357,15 +356,15 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
     }
 
     // ---------------------------------------------------------- consumers
-    const int group = warp / kRowsPerStage;
-    const int wi = warp % kRowsPerStage;
+    const int group = warp / kGroupWarps;
+    const int wi = warp % kGroupWarps;
     const int head = my_head(m.heads);
     int s = 0;
     RingCursor cursor;
     cursor.size = head >= 0 ? kAttnRingBytes : kRingBytes;
     bool ok = true;
     int prefetched_j = -1;
-    float next_scale = 0.0f;
+    float2 next_scale = make_float2(0.0f, 0.0f);
     uint32_t att_uses[2] = {0u, 0u};  // completed phases of att_bar[0 / 1]
     for (int j = 0; j < nops; ++j) {
         const MOp op = ops[j];
@@ -545,14 +544,14 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
         if (g.nblocks == 0) continue;
         // Row scales of this warp's row blocks, one lane per block, loaded
         // one linear ahead.
-        const bool rows_in_regs = g.nblocks <= 2 * 32;
-        const float row_scale = prefetched_j == j ? next_scale : load_row_scale(op, g, group, wi, lane);
+        const bool rows_in_regs = g.nblocks <= kGroups * 32;
+        const float2 row_scale = prefetched_j == j ? next_scale : load_row_scales(op, g, group, wi, lane);
         for (int j2 = j + 1; j2 < nops; ++j2) {
             const MOp op2 = ops[j2];
             if (op2.kind != kOpLinear) continue;
             const OpGeometry g2 = geometry(op2);
             if (g2.nblocks == 0) continue;
-            next_scale = load_row_scale(op2, g2, group, wi, lane);
+            next_scale = load_row_scales(op2, g2, group, wi, lane);
             prefetched_j = j2;
             break;
         }
@@ -637,12 +636,13 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
         // The word is requested now and its tag checked after the
         // quantisation, so the load's latency hides behind it.
         int64_t resid_r = -1;
-        uint64_t resid_word = 0;
-        if (op.epi == kEpiResidTagged && rows_in_regs && ok && group + 2 * lane < g.nblocks) {
-            const int64_t r = g.row0 + (int64_t)(group + 2 * lane) * kRowsPerStage + wi;
+        uint64_t resid_word0 = 0, resid_word1 = 0;
+        if (op.epi == kEpiResidTagged && rows_in_regs && ok && group + kGroups * lane < g.nblocks) {
+            const int64_t r = g.row0 + (int64_t)(group + kGroups * lane) * kRowsPerStage + 2 * wi;
             if (r < g.row1) {
                 resid_r = r;
-                resid_word = load_tagged(op.resid_ll + r);
+                resid_word0 = load_tagged(op.resid_ll + r);
+                if (r + 1 < g.row1) resid_word1 = load_tagged(op.resid_ll + r + 1);
             }
         }
         // Per-token INT8 quantisation of x (decoder.cpp:1028-1038).
@@ -669,13 +669,21 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
                                      to_code(xr[k].w, mul));
         }
         consumer_sync();
-        float row_resid = 0.0f;
+        float2 row_resid = make_float2(0.0f, 0.0f);
         if (resid_r >= 0) {
-            if (static_cast<uint32_t>(resid_word >> 32) == tag) {
-                row_resid = __uint_as_float(static_cast<uint32_t>(resid_word));
-            } else if (ok && !wait_tagged(op.resid_ll + resid_r, tag, row_resid)) {
+            if (static_cast<uint32_t>(resid_word0 >> 32) == tag) {
+                row_resid.x = __uint_as_float(static_cast<uint32_t>(resid_word0));
+            } else if (ok && !wait_tagged(op.resid_ll + resid_r, tag, row_resid.x)) {
                 ok = false;
                 *abort_flag = 1;
+            }
+            if (resid_r + 1 < g.row1) {
+                if (static_cast<uint32_t>(resid_word1 >> 32) == tag) {
+                    row_resid.y = __uint_as_float(static_cast<uint32_t>(resid_word1));
+                } else if (ok && !wait_tagged(op.resid_ll + resid_r + 1, tag, row_resid.y)) {
+                    ok = false;
+                    *abort_flag = 1;
+                }
             }
         }
         const int cols = static_cast<int>(op.cols);
@@ -684,60 +692,86 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
         for (int rb = 0; rb < g.nblocks; ++rb) {
             const int live_rows = block_rows(g, rb);
             const uint32_t start = cursor.place(static_cast<uint32_t>(live_rows * cols));
-            if ((rb & 1) != group) continue;
+            if (rb % kGroups != group) continue;
             const int st = s + rb;
             const int b = st % kStageBarriers;
             if (ok && !mbar_wait(&full[b], (st / kStageBarriers) & 1, kSiteDecodeFull)) {
                 ok = false;
                 *abort_flag = 1;
             }
-            const bool live = wi < live_rows;
-            int acc = 0, acc2 = 0;
-            if (ok && live) {
-                const uint8_t* wrow = ring + start + (size_t)wi * cols;
+            // This warp's rows 2 wi and 2 wi + 1 of the stage, side by side.
+            const bool live0 = 2 * wi < live_rows, live1 = 2 * wi + 1 < live_rows;
+            int a0 = 0, a0b = 0, a1 = 0, a1b = 0;
+            if (ok && live0) {
+                const uint8_t* w0 = ring + start + (size_t)(2 * wi) * cols;
+                if (live1) {
+                    const uint8_t* w1 = w0 + cols;
 #pragma unroll 4
-                for (int off = lane * 16; off < cols; off += 512) {
-                    const int4 wv = *reinterpret_cast<const int4*>(wrow + off);
-                    const int4 qv = *reinterpret_cast<const int4*>(codes + off);
-                    acc = dp4a(wv.x, qv.x, acc);
-                    acc2 = dp4a(wv.y, qv.y, acc2);
-                    acc = dp4a(wv.z, qv.z, acc);
-                    acc2 = dp4a(wv.w, qv.w, acc2);
+                    for (int off = lane * 16; off < cols; off += 512) {
+                        const int4 qv = *reinterpret_cast<const int4*>(codes + off);
+                        const int4 u = *reinterpret_cast<const int4*>(w0 + off);
+                        const int4 v = *reinterpret_cast<const int4*>(w1 + off);
+                        a0 = dp4a(u.x, qv.x, a0);
+                        a0b = dp4a(u.y, qv.y, a0b);
+                        a0 = dp4a(u.z, qv.z, a0);
+                        a0b = dp4a(u.w, qv.w, a0b);
+                        a1 = dp4a(v.x, qv.x, a1);
+                        a1b = dp4a(v.y, qv.y, a1b);
+                        a1 = dp4a(v.z, qv.z, a1);
+                        a1b = dp4a(v.w, qv.w, a1b);
+                    }
+                } else {
+#pragma unroll 4
+                    for (int off = lane * 16; off < cols; off += 512) {
+                        const int4 qv = *reinterpret_cast<const int4*>(codes + off);
+                        const int4 u = *reinterpret_cast<const int4*>(w0 + off);
+                        a0 = dp4a(u.x, qv.x, a0);
+                        a0b = dp4a(u.y, qv.y, a0b);
+                        a0 = dp4a(u.z, qv.z, a0);
+                        a0b = dp4a(u.w, qv.w, a0b);
+                    }
                 }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[b]);
-            acc += acc2;
+            // Both rows' sums at once: lanes 0-15 finish with row 2 wi, lanes
+            // 16-31 with row 2 wi + 1 (integer sums: any order).
+            a0 += a0b;
+            a1 += a1b;
+            const bool hi = lane >= 16;
+            int acc = (hi ? a1 : a0) + __shfl_xor_sync(0xffffffffu, hi ? a0 : a1, 16);
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-            const int64_t row = g.row0 + (int64_t)rb * kRowsPerStage + wi;
-            const float sw_rb = __shfl_sync(0xffffffffu, row_scale, (rb >> 1) & 31);
-            const float resid_rb = __shfl_sync(0xffffffffu, row_resid, (rb >> 1) & 31);
+            for (int o = 8; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+            const int64_t row = g.row0 + (int64_t)rb * kRowsPerStage + 2 * wi + (hi ? 1 : 0);
+            const int src = (rb / kGroups) & 31;
+            const float sw0 = __shfl_sync(0xffffffffu, row_scale.x, src);
+            const float sw1 = __shfl_sync(0xffffffffu, row_scale.y, src);
+            const float rs0 = __shfl_sync(0xffffffffu, row_resid.x, src);
+            const float rs1 = __shfl_sync(0xffffffffu, row_resid.y, src);
+            const bool live = hi ? live1 : live0;
             float y = 0.0f;
             if (live) {
-                const float sw = rows_in_regs ? sw_rb : __ldg(op.ws + row);
+                const float sw = rows_in_regs ? (hi ? sw1 : sw0) : __ldg(op.ws + row);
                 const float product = __fmul_rn(__int2float_rn(acc), xscale);
                 y = __fadd_rn(__fmaf_rn(product, sw, 0.0f), 0.0f);  // + (no bias)
             }
             if (op.epi == kEpiSiluPair) {
-                // Rows 2r (gate) and 2r+1 (up) sit in warps wi and wi+1.
-                float* pb = pair_y + (((rb >> 1) & 1) * 2 + group) * 8;
-                if (lane == 0) pb[wi] = y;
-                group_sync(group);
-                if (ok && live && lane == 0 && (wi & 1) == 0) {
-                    const float gate = pb[wi], up = pb[wi + 1];
+                // Rows 2 wi (gate) and 2 wi + 1 (up): lane 0 gets the up value.
+                const float up = __shfl_sync(0xffffffffu, y, 16);
+                if (ok && live0 && lane == 0) {
+                    const float gate = y;
                     const float act = __fmul_rn(up, __fdiv_rn(gate, __fadd_rn(1.0f, expf_libm(-gate, *tab_s))));
                     store_tagged(op.y_ll + row / 2, act, tag);
                 }
                 continue;
             }
-            if (!(ok && live && lane == 0)) continue;
+            if (!(ok && live && (lane & 15) == 0)) continue;
             if (op.epi == kEpiTagged) {
                 store_tagged(op.y_ll + row, y, tag);
             } else if (op.epi == kEpiResidEmbed) {
                 store_tagged(op.y_ll + row, __fadd_rn(embed_value(m, id, row), y), tag);
             } else if (op.epi == kEpiResidTagged) {
-                float hin = resid_rb;
+                float hin = hi ? rs1 : rs0;
                 if (!rows_in_regs && !wait_tagged(op.resid_ll + row, tag, hin)) {
                     ok = false;
                     *abort_flag = 1;
@@ -756,7 +790,14 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
         if (op.epi == kEpiLogits) {
             // Block argmax folded into the launch's 64-bit key: larger value
             // first, then the smaller row (std::max_element keeps the first).
+            // Lane 16's rows into lane 0's: larger value, then the smaller row.
+            const float ov = __shfl_sync(0xffffffffu, best, 16);
+            const int32_t orow = __shfl_sync(0xffffffffu, best_r, 16);
             if (lane == 0) {
+                if (orow != 0x7fffffff && (best_r == 0x7fffffff || ov > best || (ov == best && orow < best_r))) {
+                    best = ov;
+                    best_r = orow;
+                }
                 best_v[warp] = best;
                 best_row[warp] = best_r;
             }
