@@ -373,9 +373,12 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
             // ---------------------------------------------- attention
             // Cached keys / values of rows [0, pos) are staged through the
             // attention region (the ring's last 64 KB, the codes buffer and
-            // the scratch: free in this block now) in chunks of C rows, one
-            // bulk copy per chunk; chunk 0 of both is requested before the
-            // wait for this token's q, k, v.
+            // the scratch: free in this block now) in chunks of C rows; chunk
+            // 0 of both is requested before the wait for this token's q, k, v.
+            // Values come in one bulk copy per chunk.  Keys come as 16-byte
+            // asynchronous copies by all consumer threads into rows padded by
+            // 4 floats, so the 8 lanes of a quarter warp, each reading a float4
+            // of its own key, hit 8 different bank groups.
             const int dim = m.dim, half = dim / 2;
             const int kvh = head / (m.heads / m.kv_heads);
             float* qs = qkv_s;
@@ -387,9 +390,10 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
             float* att = reinterpret_cast<float*>(ring + kAttnRingBytes);
             const int keys_r = static_cast<int>((keys + 3) & ~3);
             float* scores = att;
-            const int chunk = static_cast<int>(min64((kAttFloats - keys_r) / (2 * dim), pos > 0 ? pos : 1));
+            const int kst = dim + 4;  // padded key row (floats)
+            const int chunk = static_cast<int>(min64((kAttFloats - keys_r) / (kst + dim), pos > 0 ? pos : 1));
             float* kbuf = att + keys_r;
-            float* vbuf = kbuf + chunk * dim;
+            float* vbuf = kbuf + chunk * kst;
             const uint64_t keep = l2_policy_evict_last();
             const int nchunks = static_cast<int>((pos + chunk - 1) / chunk);
             auto issue = [&](const float* base, float* dst, uint64_t* bar, int c) {
@@ -398,11 +402,19 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
                 mbar_arrive_expect_tx(bar, bytes);
                 bulk_copy_g2s(dst, base + k0 * dim, bytes, bar, keep);
             };
+            auto load_keys = [&](int c) {  // every consumer thread; completed by wait_async_copies()
+                const int64_t k0 = (int64_t)c * chunk;
+                const int rows = static_cast<int>(min64(chunk, pos - k0));
+                const int vpr = dim / 4;
+                for (int i = tid; i < rows * vpr; i += kNC) {
+                    const int r = i / vpr, q = i - r * vpr;
+                    async_copy16(kbuf + (size_t)r * kst + 4 * q, kc + (k0 + r) * dim + 4 * q);
+                }
+                commit_async_copies();
+            };
             consumer_sync();  // every warp is done with the previous linear's codes
-            if (tid == 0 && nchunks > 0) {
-                issue(kc, kbuf, &att_bar[0], 0);
-                issue(vc, vbuf, &att_bar[1], 0);
-            }
+            if (nchunks > 0) load_keys(0);
+            if (tid == 0 && nchunks > 0) issue(vc, vbuf, &att_bar[1], 0);
             // This position's rotation (independent of q and k), before the wait.
             float rope_c = 0.0f, rope_s = 0.0f;
             if (tid < half) {
@@ -450,15 +462,12 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
             for (int c = 0; c < nchunks; ++c) {
                 const int64_t k0 = (int64_t)c * chunk;
                 const int nk = static_cast<int>(min64(chunk, pos - k0));
-                if (c > 0 && tid == 0) issue(kc, kbuf, &att_bar[0], c);
-                if (ok && !mbar_wait(&att_bar[0], att_uses[0] & 1, kSiteDecodeFull)) {
-                    ok = false;
-                    *abort_flag = 1;
-                }
-                ++att_uses[0];
+                if (c > 0) load_keys(c);
+                wait_async_copies();
+                consumer_sync();
                 for (int k = tid; k < nk; k += kNC) {
                     if (!ok) break;
-                    const float* krow = kbuf + k * dim;
+                    const float* krow = kbuf + k * kst;
                     float dot = 0.0f;
                     for (int d = 0; d < dim; d += 4) {
                         const float4 kv = *reinterpret_cast<const float4*>(krow + d);
@@ -512,7 +521,9 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
                 ++att_uses[1];
                 if (ok && tid < dim) {
                     const float* vb = vbuf + tid;
-                    for (int k = 0; k < nk; ++k) acc = __fadd_rn(acc, __fmul_rn(scores[k0 + k], vb[k * dim]));
+                    const float* pk = scores + k0;
+#pragma unroll 8
+                    for (int k = 0; k < nk; ++k) acc = __fadd_rn(acc, __fmul_rn(pk[k], vb[k * dim]));
                 }
                 consumer_sync();  // chunk consumed
             }
