@@ -82,6 +82,7 @@ def _case_weight(rows, cols, bits, group, device):
 
 # name: (tokens, rows, cols, weight bits, group, activation bits)
 CASES = {
+    "gemv0": (1, 5632, 2048, 8, 2048, 8),       # config 0 decode GEMV, 11.5 MB
     "gemv": (1, 11264, 2048, 8, 2048, 8),       # gate|up decode GEMV, 23 MB
     "lmhead": (1, 32000, 2048, 8, 2048, 8),     # lm_head decode GEMV, 65.5 MB
     "gemm": (512, 5632, 2048, 8, 2048, 8),      # config 2 prefill GEMM
@@ -179,6 +180,13 @@ def measured_peaks():
         data = json.loads(path.read_text())
         return float(data["hbm_gbs"]), "measured"
     return FALLBACK_HBM_GBS, "fallback"
+
+
+def measured_bf16_tflops():
+    path = REPO / "MEASURED_PEAKS.json"
+    if path.exists():
+        return float(json.loads(path.read_text())["bf16_tflops"])
+    return 1590.0  # fallback burst figure
 
 
 PROMPT = 128   # config 3: 128 random prompt ids, then 128 greedy tokens
@@ -382,6 +390,8 @@ def run_ours(args, rank, world, local_rank):
     if lib.leafq_device_status() != 0:
         raise RuntimeError(f"device status: {lib.leafq_last_error().decode()}")
 
+    rates = linear_rates(device, measured_peaks()[0])
+
     out_dir = REPO / "gpurun_out"
     out_dir.mkdir(exist_ok=True)
     visible = [v for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
@@ -471,11 +481,97 @@ def run_ours(args, rank, world, local_rank):
                     "ms_per_step": e2e_ms_step},
             "gpu_launches": args.steps,
             "per_operator_graph_us_per_token": per_op_us,
+            "linear_rates": rates,
             "clocks": clocks,
             "cpu_baseline": cpu,
             "when": datetime.datetime.now(datetime.timezone.utc).isoformat(timespec="seconds"),
         }
         print(json.dumps(line), flush=True)
+
+
+GEMV_COPIES = 32  # distinct config-0 weights per replay: 32 x 11.5 MB > L2
+
+
+def linear_rates(device, peak_gbs):
+    """Configs 0 and 2 as figures beside the headline step.
+
+    Config 0 (W8A8 GEMV, M=1, K=2048, N=5632, bias): GEMV_COPIES distinct
+    seeded weights, one leafq_linear each with programmatic dependent launch
+    (each launch streams its weights while the previous one finishes),
+    captured in a CUDA graph and replayed; per-GEMV time = graph time /
+    GEMV_COPIES.  The lm_head shape (N=32000) the same way with 4 copies.
+    Config 2 (W8A8 prefill GEMM, M=512 tokens with 1% outliers x20,
+    K=2048, N=5632 and K=5632, N=2048): 8 launches per graph on distinct
+    weights, activation quantisation included."""
+    import torch
+
+    import leaf_b200 as lq
+    from leaf_b200._lib import LEAFQ_FLAG_PDL
+    from leaf_b200.stack import random_w8_weight
+
+    gen = torch.Generator(device=device)
+    gen.manual_seed(7)
+    stream = torch.cuda.current_stream(device)
+
+    def timed(calls, reps=10):
+        for fn in calls:
+            fn()
+        torch.cuda.synchronize(device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for fn in calls:
+                fn()
+        for _ in range(3):
+            graph.replay()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        b.record(stream)
+        torch.cuda.synchronize(device)
+        del graph
+        return a.elapsed_time(b) * 1e3 / (reps * len(calls))  # us per call
+
+    out = {}
+    ws = lq.Workspace(device)
+    for name, rows, cols, copies in (("gemv_config0", 5632, 2048, GEMV_COPIES), ("gemv_lm_head", 32000, 2048, 4)):
+        weights = []
+        for _ in range(copies):
+            w = random_w8_weight(rows, cols, gen, device)
+            w.bias = torch.randn(rows, generator=gen, device=device) * 0.01
+            weights.append(w)
+        x = torch.randn(1, cols, generator=gen, device=device)
+        ys = [torch.empty(1, rows, device=device) for _ in weights]
+        us = timed([lambda w=w, y=y: lq.linear(x, w, out=y, workspace=ws, flags=LEAFQ_FLAG_PDL)
+                    for w, y in zip(weights, ys)])
+        nbytes = rows * cols + 4 * rows + 4 * rows + 4 * cols + 4 * rows  # W, scales, bias, x, y
+        gbs = nbytes / (us * 1e-6) / 1e9
+        out[name] = {"rows": rows, "cols": cols, "us_per_call": us, "achieved": gbs, "unit": "GB/s",
+                     "peak": peak_gbs, "frac": gbs / peak_gbs, "bytes_per_call": nbytes,
+                     "method": f"{copies} distinct weights (> L2) back to back with PDL in one CUDA graph, "
+                               "CUDA events"}
+        del weights, ys
+        torch.cuda.empty_cache()
+    peak_top = 2.0 * measured_bf16_tflops()
+    tokens = 512
+    xg = torch.randn(tokens, 5632, generator=gen, device=device)
+    mask = torch.rand(tokens, 5632, generator=gen, device=device) < 0.01
+    xg = torch.where(mask, xg * 20.0, xg)
+    for n, k in ((5632, 2048), (2048, 5632)):
+        wl = [random_w8_weight(n, k, gen, device) for _ in range(8)]
+        xk = xg[:, :k].contiguous()
+        yl = [torch.empty(tokens, n, device=device) for _ in wl]
+        us = timed([lambda w=w, y=y: lq.linear(xk, w, out=y, workspace=ws, flags=LEAFQ_FLAG_PDL)
+                    for w, y in zip(wl, yl)])
+        tops = 2.0 * tokens * n * k / (us * 1e-6) / 1e12
+        out[f"gemm_config2_n{n}_k{k}"] = {"us_per_call": us, "achieved": tops, "unit": "TOP/s", "peak": peak_top,
+                                          "frac": tops / peak_top,
+                                          "peak_source": "2 x measured bf16 burst (no INT8 figure measured)",
+                                          "method": "8 distinct weights back to back in one CUDA graph "
+                                                    "(activation quantisation included)"}
+        del wl, yl
+    torch.cuda.empty_cache()
+    return out
 
 
 BATCH_SEQUENCES, BATCH_PROMPT, BATCH_GENERATED = 64, 512, 256  # config 4
