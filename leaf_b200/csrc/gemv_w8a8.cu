@@ -4,22 +4,25 @@
 // quantisation, :1221-1231 with quant_dot_avx :536-570) for per-row INT8
 // weights (group == cols, the default export) and 1..8 tokens.
 //
-// Layout of one block (one per SM, ~200 KB of shared memory):
+// Layout of one block (two per SM, up to 100 KB of shared memory each):
 //   warp 8 (producer): streams this block's contiguous slice of weight rows
 //     into a ring of stages with 1-D bulk copies (cp.async.bulk, TMA engine,
-//     evict-first L2 policy).  A stage holds one chunk (<= 4 KB) of 8 rows.
+//     evict-first L2 policy).  A stage holds one chunk (<= 2 KB) of 16 rows.
 //     Weight loads are issued before the kernel waits on the previous grid
 //     (programmatic dependent launch), so the stream starts while the
 //     producer of x is still finishing.
 //   warps 0-7 (consumers): wait for x, compute each token's absmax and
 //     scale redundantly per block (x is a few KB, L2-resident), write int8
-//     codes to shared memory, then each warp takes one row of every stage:
-//     lanes read 16 weight bytes and 16 code bytes per step and accumulate
-//     with dp4a.  int32 sums are exact in any order; a warp reduction gives
-//     the row sum and lane t finishes token t:
+//     codes to shared memory, then each warp takes two rows of every stage
+//     side by side: lanes read 16 bytes of each row and 16 code bytes per
+//     step and accumulate with dp4a.  int32 sums are exact in any order; one
+//     warp reduction gives both rows' sums and lanes t / 16 + t finish token
+//     t of the two rows:
 //       y = fma(float(acc) * sx, sw, 0.0f) + (bias or 0.0f)
 //     which is the reference's result[t] += float(acc) * sx * sw (fused by
 //     GCC into one FMA, decoder.cpp:567) followed by + bias (:1229).
+//   Two blocks per SM (half the shared memory each), so twice the warps
+//   hide the per-row latency of the dot, reduction and epilogue.
 // Bytes per call: rows * cols (weights) + 4 * rows (scales) [+ 4 * rows bias]
 //   + 4 * tokens * (cols + rows): HBM-bound.
 #include "leafq_device.cuh"
@@ -29,9 +32,9 @@ namespace leafq {
 namespace {
 
 constexpr int kConsumerWarps = 8;
-constexpr int kRowsPerStage = kConsumerWarps;
+constexpr int kRowsPerStage = 2 * kConsumerWarps;  // warp w owns rows 2w and 2w + 1 of a stage
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
-constexpr int kChunkMax = 4096;
+constexpr int kChunkMax = 2048;
 // About half an SM's shared memory, so that under programmatic dependent
 // launch the next GEMV's block fits beside this one and starts its weight
 // stream before this one ends.  96 KB in flight per SM is still well above
@@ -66,7 +69,7 @@ __device__ __forceinline__ int8_t to_code(float v, float multiplier) {
 }
 
 template <int MAXT>
-__global__ void __launch_bounds__(kThreads, 1) gemv_w8a8_kernel(const GemvArgs a) {
+__global__ void __launch_bounds__(kThreads, 2) gemv_w8a8_kernel(const GemvArgs a) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const int S = a.stages;
     const int chunk = a.chunk;
@@ -120,13 +123,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_w8a8_kernel(const GemvArgs a
     const int nthreads = kConsumerWarps * 32;
     // Weight scales and bias are read-only: fetch this warp's rows (row
     // row0 + 8 * rb + warp sits in lane rb) before waiting for x.
-    float row_scale = 0.0f, row_bias = 0.0f;
+    float2 row_scale = make_float2(0.0f, 0.0f), row_bias = make_float2(0.0f, 0.0f);
     const bool rows_in_regs = nblocks <= 32;
     if (rows_in_regs && lane < nblocks) {
-        const int64_t r = row0 + (int64_t)lane * kRowsPerStage + warp;
+        const int64_t r = row0 + (int64_t)lane * kRowsPerStage + 2 * warp;
         if (r < row1) {
-            row_scale = __ldg(a.ws + r);
-            row_bias = a.bias ? __ldg(a.bias + r) : 0.0f;
+            row_scale.x = __ldg(a.ws + r);
+            row_bias.x = a.bias ? __ldg(a.bias + r) : 0.0f;
+        }
+        if (r + 1 < row1) {
+            row_scale.y = __ldg(a.ws + r + 1);
+            row_bias.y = a.bias ? __ldg(a.bias + r + 1) : 0.0f;
         }
     }
     grid_dependency_wait();
@@ -204,58 +211,74 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_w8a8_kernel(const GemvArgs a
     }
     consumer_sync();
 
-    // Main loop: warp `warp` owns row (row0 + 8 * rb + warp) of every stage.
+    // Main loop: warp `warp` owns rows row0 + 16 rb + 2 warp and the next of
+    // every stage, side by side (two independent chains per lane).
     for (int rb = 0; rb < nblocks; ++rb) {
-        const int64_t row = row0 + (int64_t)rb * kRowsPerStage + warp;
-        const bool live = row < row1;
-        int acc[MAXT];
+        const int64_t rowa = row0 + (int64_t)rb * kRowsPerStage + 2 * warp;
+        const bool live0 = rowa < row1, live1 = rowa + 1 < row1;
+        int acc0[MAXT], acc1[MAXT];
 #pragma unroll
-        for (int t = 0; t < MAXT; ++t) acc[t] = 0;
+        for (int t = 0; t < MAXT; ++t) acc0[t] = acc1[t] = 0;
         for (int c = 0; c < a.nchunks; ++c) {
             const int s = rb * a.nchunks + c;
             const int buf = s % S;
             if (!mbar_wait(&full[buf], (s / S) & 1, kSiteGemvFull)) return;
-            if (live) {
-                const uint8_t* wrow = stage_base + ((size_t)buf * kRowsPerStage + warp) * chunk;
+            if (live0) {
+                const uint8_t* w0 = stage_base + ((size_t)buf * kRowsPerStage + 2 * warp) * chunk;
+                const uint8_t* w1 = w0 + chunk;
                 const int64_t cbeg = (int64_t)c * chunk;
                 const int cb = static_cast<int>(min64(chunk, a.cols - cbeg));
                 const int8_t* crow = codes + cbeg;
 #pragma unroll 4
                 for (int off = lane * 16; off < cb; off += 512) {
-                    const int4 wv = *reinterpret_cast<const int4*>(wrow + off);
+                    const int4 u = *reinterpret_cast<const int4*>(w0 + off);
+                    const int4 v = live1 ? *reinterpret_cast<const int4*>(w1 + off) : make_int4(0, 0, 0, 0);
 #pragma unroll
                     for (int t = 0; t < MAXT; ++t) {
                         const int4 qv = *reinterpret_cast<const int4*>(crow + t * a.qstride + off);
-                        acc[t] = dp4a(wv.x, qv.x, acc[t]);
-                        acc[t] = dp4a(wv.y, qv.y, acc[t]);
-                        acc[t] = dp4a(wv.z, qv.z, acc[t]);
-                        acc[t] = dp4a(wv.w, qv.w, acc[t]);
+                        acc0[t] = dp4a(u.x, qv.x, acc0[t]);
+                        acc1[t] = dp4a(v.x, qv.x, acc1[t]);
+                        acc0[t] = dp4a(u.y, qv.y, acc0[t]);
+                        acc1[t] = dp4a(v.y, qv.y, acc1[t]);
+                        acc0[t] = dp4a(u.z, qv.z, acc0[t]);
+                        acc1[t] = dp4a(v.z, qv.z, acc1[t]);
+                        acc0[t] = dp4a(u.w, qv.w, acc0[t]);
+                        acc1[t] = dp4a(v.w, qv.w, acc1[t]);
                     }
                 }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[buf]);
         }
-        const float sw_rb = __shfl_sync(0xffffffffu, row_scale, rb & 31);
-        const float bias_rb = __shfl_sync(0xffffffffu, row_bias, rb & 31);
-        if (live) {
+        const float2 sw_rb = make_float2(__shfl_sync(0xffffffffu, row_scale.x, rb & 31),
+                                         __shfl_sync(0xffffffffu, row_scale.y, rb & 31));
+        const float2 bias_rb = make_float2(__shfl_sync(0xffffffffu, row_bias.x, rb & 31),
+                                           __shfl_sync(0xffffffffu, row_bias.y, rb & 31));
+        if (live0) {
+            // Both rows at once (integer sums: any order): lanes 0-15 finish
+            // with row 2 warp, lanes 16-31 with the next; lane t and lane
+            // 16 + t then hold token t's sums.
+            const bool hi = lane >= 16;
             int mine = 0;
 #pragma unroll
             for (int t = 0; t < MAXT; ++t) {
+                int v = (hi ? acc1[t] : acc0[t]) + __shfl_xor_sync(0xffffffffu, hi ? acc0[t] : acc1[t], 16);
 #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], o);
-                if (lane == t) mine = acc[t];
+                for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                if ((lane & 15) == t) mine = v;
             }
-            if (lane < a.tokens) {
-                const float sw = rows_in_regs ? sw_rb : __ldg(a.ws + row);
-                const float bias = rows_in_regs ? bias_rb : (a.bias ? __ldg(a.bias + row) : 0.0f);
-                const float product = __fmul_rn(__int2float_rn(mine), token_scale[lane]);
+            const int tok = lane & 15;
+            const int64_t row = rowa + (hi ? 1 : 0);
+            if (tok < a.tokens && (hi ? live1 : true)) {
+                const float sw = rows_in_regs ? (hi ? sw_rb.y : sw_rb.x) : __ldg(a.ws + row);
+                const float bias = rows_in_regs ? (hi ? bias_rb.y : bias_rb.x) : (a.bias ? __ldg(a.bias + row) : 0.0f);
+                const float product = __fmul_rn(__int2float_rn(mine), token_scale[tok]);
                 const float result = __fmaf_rn(product, sw, 0.0f);
                 const float y = __fadd_rn(result, bias);
                 if (a.peer.world)
-                    peer_store(a.peer, tag, lane, row, y);
+                    peer_store(a.peer, tag, tok, row, y);
                 else
-                    a.y[(int64_t)lane * a.rows + row] = y;
+                    a.y[(int64_t)tok * a.rows + row] = y;
             }
         }
     }
@@ -300,7 +323,9 @@ int launch_gemv_w8a8(cudaStream_t s, const float* x, int64_t tokens, int64_t col
     const int maxt = tokens <= 1 ? 1 : tokens <= 2 ? 2 : tokens <= 4 ? 4 : 8;
     a.qstride = static_cast<int>((cols + 15) / 16 * 16);
     const int64_t blocks_needed = (rows + kRowsPerStage - 1) / kRowsPerStage;
-    const int grid = static_cast<int>(std::min<int64_t>(sm_count(), blocks_needed));
+    // Two blocks per SM: twice the consumer warps to hide the per-row
+    // latency of the dot, reduction and epilogue.
+    const int grid = static_cast<int>(std::min<int64_t>(2 * sm_count(), blocks_needed));
     // Stages needed by the largest block, and what fits next to the codes.
     const int64_t max_rows = (rows + grid - 1) / grid;
     const int64_t max_stages = ((max_rows + kRowsPerStage - 1) / kRowsPerStage) * a.nchunks;
