@@ -560,6 +560,25 @@ class Decoder:
         (one launch); the argmax replaces self.token."""
         check(self.lib.leafq_model_plan_run(_stream(), self._plan))
 
+    def capture_stream_step(self, token_in: torch.Tensor, token_out: torch.Tensor) -> "torch.cuda.CUDAGraph":
+        """One streaming decode step as a CUDA graph, for a server that sends
+        every token to its client: copy the input token id from pinned host
+        memory (``token_in``, int32 [1]), run step_fused(), copy the produced
+        token id into pinned host memory (``token_out``).  Replay it, then
+        synchronise the stream before reading ``token_out``.  The graph holds
+        the plan's buffers: delete it before close()."""
+        if self._plan is None:
+            self.build_fused()
+        for t in (token_in, token_out):
+            if t.device.type != "cpu" or not t.is_pinned() or t.dtype != torch.int32 or t.numel() != 1:
+                raise LeafError(_lib.LEAFQ_ERR_INVALID, "stream tokens must be pinned int32 [1] host tensors")
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            self.token.copy_(token_in, non_blocking=True)
+            self.step_fused()
+            token_out.copy_(self.token, non_blocking=True)
+        return graph
+
     def generate_fused(self, prompt, max_new: int) -> list[int]:
         """Greedy continuation as generate(), with every decode step one
         launch of the whole-model kernel."""

@@ -78,6 +78,36 @@ def test_tiny_fused_decode_step(cuda_device, tmp_path):
     dec.close()
 
 
+def test_tiny_stream_step_graph(cuda_device, tmp_path):
+    """The streaming-step graph (token in from pinned host memory, the fused
+    step, token out to pinned host memory) gives the reference's tokens."""
+    import torch
+
+    from leaf_b200.decoder import Decoder
+
+    path, golden = _artifact(tmp_path, "tiny_w8", fx.TINY)
+    dec = Decoder(path)
+    prompt, generated = golden["prompt"].tolist(), golden["generated"].tolist()
+    logits = dec.forward(prompt)
+    first = int(np.argmax(logits.cpu().numpy().reshape(-1, dec.cfg.vocab)[-1]))
+    assert first == generated[0]
+    tok_in = torch.empty(1, dtype=torch.int32).pin_memory()
+    tok_out = torch.empty(1, dtype=torch.int32).pin_memory()
+    graph = dec.capture_stream_step(tok_in, tok_out)
+    tok_in[0] = first
+    got = [first]
+    stream = torch.cuda.current_stream()
+    for _ in generated[1:]:
+        graph.replay()
+        stream.synchronize()
+        got.append(int(tok_out[0]))
+        tok_in.copy_(tok_out)
+    assert got == generated
+    assert dec.device_status() == 0
+    del graph
+    dec.close()
+
+
 def test_tinyllama_greedy_tokens(cuda_device, tmp_path):
     """Config 3: TinyLlama-1.1B-shape W8A8 decoder, 128-token random prompt,
     128 greedy tokens, identical to the reference's."""
