@@ -300,8 +300,10 @@ typedef struct leafq_model_desc {
 
 typedef struct leafq_model_plan_t leafq_model_plan_t;
 
-/* Checks the geometry, allocates the plan's hand-off buffers on the current
- * device and records the op list; pointers in desc must stay valid. */
+/* Checks the geometry (hidden <= 4096, intermediate <= 6144, both multiples
+ * of 16; wider models use the per-operator entry points), allocates the
+ * plan's hand-off buffers on the current device and records the op list;
+ * pointers in desc must stay valid. */
 int leafq_model_plan_create(const leafq_model_desc* desc, leafq_model_plan_t** plan);
 /* One decode step (one cooperative launch of one block per SM). */
 int leafq_model_plan_run(void* stream, leafq_model_plan_t* plan);

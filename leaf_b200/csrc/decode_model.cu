@@ -55,7 +55,7 @@ constexpr uint32_t kRingBytes = 192 * 1024;
 // codes buffer and the scratch behind it, 88 KB of keys / values / scores.
 constexpr uint32_t kAttnRingBytes = 128 * 1024;
 constexpr int kStageBarriers = 16;
-constexpr int kMaxCols = 8192;
+constexpr int kMaxCols = 6144;  // widest linear input (TinyLlama's 5632); x stays in registers
 constexpr int kXVec = kMaxCols / 4 / kNC;
 constexpr int kScratchFloats = 4096;  // hidden row for RMSNorm; attention scores + V chunk
 constexpr int kNormXVec = kScratchFloats / 4 / kNC;  // float4s of a normalised (hidden) row per thread
@@ -154,7 +154,7 @@ __device__ __forceinline__ bool load_tagged_x(const uint64_t* x, int64_t vecs, u
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
             const int64_t i = tid + (int64_t)(k0 + k) * kNC;
-            if (i < vecs) {
+            if (k0 + k < kXVec && i < vecs) {
                 load_tagged2(x + 4 * i, w[k][0], w[k][1]);
                 load_tagged2(x + 4 * i + 2, w[k][2], w[k][3]);
             } else {
@@ -163,6 +163,7 @@ __device__ __forceinline__ bool load_tagged_x(const uint64_t* x, int64_t vecs, u
         }
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
+            if (k0 + k >= kXVec) break;
             const int64_t i = tid + (int64_t)(k0 + k) * kNC;
             auto all_tagged = [&]() {
                 return static_cast<uint32_t>(w[k][0] >> 32) == tag && static_cast<uint32_t>(w[k][1] >> 32) == tag &&
@@ -887,7 +888,7 @@ int leafq_model_plan_create(const leafq_model_desc* d, leafq_model_plan_t** out)
         h > kMaxCols || 5 * d->layers + 1 > kMaxOps || d->heads > sm_count() ||
         !(d->attn_scale > 0.0f)) {
         set_error("leafq_model_plan_create: unsupported geometry (hidden and intermediate multiples of "
-                  "16 and <= 4096 / 8192, heads * head_dim == hidden, head_dim a multiple of 4 and <= 256, "
+                  "16 and <= 4096 / 6144, heads * head_dim == hidden, head_dim a multiple of 4 and <= 256, "
                   "capacity <= 2048, heads <= SMs)");
         return LEAFQ_ERR_UNSUPPORTED;
     }
