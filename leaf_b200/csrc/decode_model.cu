@@ -19,9 +19,12 @@
 //   0), which every block computes for itself -- identical in every block --
 //   before quantising it.  Epilogues write tagged outputs: plain, residual
 //   (h + y, the residual read from the tagged hidden vector), the SiLU gate
-//   (gate and up rows are interleaved, so a row pair meets in one stage and
-//   two warps exchange it through shared memory), or logits plus a
-//   block-local argmax folded into one 64-bit atomicMax key.
+//   (gate and up rows are interleaved, and each consumer warp takes two
+//   rows of a stage, so a row pair meets in one warp), or logits plus a
+//   block-local argmax folded into one 64-bit atomicMax key.  The 16
+//   consumer warps form four groups of four; group q takes the stages
+//   rb % 4 == q.  RMSNorm's sum of squares runs on all consumer threads
+//   (sum_in_order_par), bit-identical to the reference's sequential sum.
 // * Attention for query head h runs in block h * G / heads: it reads the
 //   tagged q, k, v of this token, applies RoPE from the host tables, appends
 //   k, v to the layer's cache (one block per KV head), and attends over the
