@@ -244,15 +244,27 @@ def cpu_reference_decoder(threads: int, new_tokens: int, warmup: int = 0, prompt
 
 
 # ----------------------------------------------------------------- clocks
+def smi_index(local_rank, device):
+    """nvidia-smi's index of this rank's GPU (CUDA_VISIBLE_DEVICES maps it)."""
+    visible = [v for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+    return visible[local_rank] if local_rank < len(visible) else str(device.index)
+
+
 class ClockSampler:
-    def __init__(self, index: int, path: Path):
-        self.path = path
+    """nvidia-smi clock / throttle samples every 100 ms while the timed region
+    runs, written to a file in a private temporary directory."""
+
+    def __init__(self, index, name: str):
+        import tempfile
+
+        self.dir = tempfile.TemporaryDirectory(prefix="leafq_clocks_")
+        self.path = Path(self.dir.name) / name
         self.proc = None
         query = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
                  "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
-            self.file = open(path, "w")
+            self.file = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={index}", f"--query-gpu={query}", "--format=csv,noheader,nounits",
                  "-lms", "100"], stdout=self.file, stderr=subprocess.DEVNULL)
@@ -273,6 +285,7 @@ class ClockSampler:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) >= 9:
                 rows.append(parts)
+        self.dir.cleanup()
         if not rows:
             return None
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
@@ -392,11 +405,7 @@ def run_ours(args, rank, world, local_rank):
 
     rates = linear_rates(device, measured_peaks()[0])
 
-    out_dir = REPO / "gpurun_out"
-    out_dir.mkdir(exist_ok=True)
-    visible = [v for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
-    smi_id = visible[local_rank] if local_rank < len(visible) else str(device.index)
-    sampler = ClockSampler(smi_id, out_dir / f"clocks_rank{rank}.csv")
+    sampler = ClockSampler(smi_index(local_rank, device), f"clocks_rank{rank}.csv")
     time.sleep(0.3)
     # ------------------------------------------------ device-timed value
     barrier()
@@ -447,7 +456,26 @@ def run_ours(args, rank, world, local_rank):
     if status != 0:
         raise RuntimeError(f"device status {status}: {lib.leafq_last_error().decode()}")
     del step_graph
+    # Rank 0's greedy tokens after its prompt (model seed 1234, prompt seed
+    # 99): the unsharded answer the row-sharded runs at N > 1 must give.
+    rewind()
+    for _ in range(TP_TOKENS - 1):
+        dec.step_fused()
+    replica_tokens = [int(first.item())] + [int(t) for t in dec.history[PROMPT + 1:PROMPT + TP_TOKENS].tolist()]
     dec.close()
+    del dec
+    torch.cuda.empty_cache()
+
+    extra = {}
+    if world == 1:
+        # Config 4 (64 x 512-token prompts) on this GPU beside the headline.
+        c4 = batch_run("dp", "nccl", 1, rank, device, BATCH_LINE_STEPS, args.warmup)
+        c4.pop("_tokens")
+        extra["config4"] = dict(c4, workload=f"config 4: {BATCH_SEQUENCES} sequences x {BATCH_PROMPT}-token "
+                                             f"random prompts decoded together on one GPU, "
+                                             f"{BATCH_LINE_STEPS} greedy decode steps timed")
+    else:
+        extra.update(multi_gpu_paths(args, rank, world, device, replica_tokens))
 
     ms_step = ms_total / args.steps
     value = world * 1000.0 / ms_step
@@ -456,7 +484,7 @@ def run_ours(args, rank, world, local_rank):
     positions = [PROMPT + (i % (GENERATED - 1)) for i in range(args.steps)]
     step_bytes = float(np.mean([decoder_step_bytes(shape, p) for p in positions]))
     achieved = step_bytes / (ms_step * 1e-3) / 1e9
-    traffic = read_traffic()
+    traffic = DECODE_TRAFFIC_RATIO * step_bytes
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -491,22 +519,175 @@ def run_ours(args, rank, world, local_rank):
             "linear_rates": rates,
             "clocks": clocks,
             "cpu_baseline": cpu,
+            **extra,
             "when": datetime.datetime.now(datetime.timezone.utc).isoformat(timespec="seconds"),
         }
         print(json.dumps(line), flush=True)
+
+
+TP_TOKENS = 17  # greedy tokens compared between the sharded and unsharded config-3 decoders
+TP_STEPS = 64   # config-3 tp decode steps timed
+
+
+def config3_tp_run(world, rank, device, warmup):
+    """Config 3 (batch 1, 128-token prompt) with every linear's rows split
+    over the ranks and each decode-step output gathered by the library's
+    peer-memory all-gather inside the step's CUDA graph (per-operator
+    kernels).  Model seed 1234 and prompt seed 99 on every rank: rank 0's
+    replica decoded the same request unsharded.  Returns (tokens/s, tokens)."""
+    import torch
+    import torch.distributed as dist
+
+    import leaf_b200 as lq
+    from leaf_b200._lib import check
+    from leaf_b200.decoder import Decoder
+    from leaf_b200.stack import RandomDecoderModel, StackShape
+
+    shape = StackShape()
+    model = RandomDecoderModel(shape, seed=1234, device=device)
+    dec = Decoder(model, device=device, group=dist.group.WORLD, gather="peer")
+    model.release()
+    del model
+    gen = torch.Generator().manual_seed(99)
+    prompt = torch.randint(0, shape.vocab, (PROMPT,), generator=gen).tolist()
+    dec.capture_decode()
+    tokens = dec.generate(prompt, TP_TOKENS)
+    stream = torch.cuda.current_stream(device)
+    dec.reset()
+    logits = dec.forward(prompt)
+    check(lq.load().leafq_argmax(stream.cuda_stream, logits.data_ptr(), 1, shape.vocab,
+                                 dec._bufs(1)["ids"].data_ptr()))
+    for _ in range(max(warmup, 3)):
+        dec._decode_step()
+    torch.cuda.synchronize(device)
+    _barrier(world)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(TP_STEPS):
+        dec._decode_step()
+    b.record(stream)
+    torch.cuda.synchronize(device)
+    _barrier(world)
+    ms = _max_over_ranks(a.elapsed_time(b), world, device)
+    status = lq.load().leafq_device_status()
+    if status != 0:
+        raise RuntimeError(f"device status {status}: {lq.load().leafq_last_error().decode()}")
+    dec.close()
+    del dec
+    torch.cuda.empty_cache()
+    return TP_STEPS / (ms * 1e-3), tokens
+
+
+def gather_timing(world, device):
+    """Microseconds per all-gather of one decode-step output ([tokens, rows]
+    fp32, rows split evenly over the ranks): the library's peer-memory
+    gather (send + collect kernels, 20 per CUDA graph, replayed) and NCCL's
+    all_gather_into_tensor (eager); max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from leaf_b200.parallel import PeerAllGather
+
+    rank = dist.get_rank()
+    stream = torch.cuda.current_stream(device)
+    out = {}
+    shapes = ((1, 2048), (1, 11264), (64, 2048), (64, 11264))
+    peer = PeerAllGather(max(t * r for t, r in shapes))
+    try:
+        for tokens, rows in shapes:
+            n = rows // world
+            local = torch.randn(tokens, n, device=device)
+            full = torch.empty(tokens, rows, device=device)
+            for _ in range(3):
+                peer.run(local, rank * n, rows, full)
+            torch.cuda.synchronize(device)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for _ in range(20):
+                    peer.run(local, rank * n, rows, full)
+            graph.replay()
+            torch.cuda.synchronize(device)
+            _barrier(world)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            for _ in range(10):
+                graph.replay()
+            b.record(stream)
+            torch.cuda.synchronize(device)
+            peer_us = _max_over_ranks(a.elapsed_time(b) * 1e3 / 200, world, device)
+            del graph
+            flat = torch.empty(tokens * rows, device=device)
+            for _ in range(3):
+                dist.all_gather_into_tensor(flat, local.reshape(-1))
+            torch.cuda.synchronize(device)
+            _barrier(world)
+            a.record(stream)
+            for _ in range(50):
+                dist.all_gather_into_tensor(flat, local.reshape(-1))
+            b.record(stream)
+            torch.cuda.synchronize(device)
+            nccl_us = _max_over_ranks(a.elapsed_time(b) * 1e3 / 50, world, device)
+            out[f"{tokens}x{rows}"] = {"peer_us": peer_us, "nccl_us": nccl_us, "bytes": tokens * rows * 4}
+    finally:
+        peer.close()
+    return out
+
+
+def multi_gpu_paths(args, rank, world, device, replica_tokens):
+    """The row-sharded (tp) and sequence-split (dp) paths of configs 3 and 4
+    on this job's N GPUs, beside the replica value, with a parity check:
+    every sharded run's greedy tokens against unsharded runs of the same
+    requests (config 4: the dp run, whose ranks hold full weights; config 3:
+    rank 0's replica)."""
+    import torch
+    import torch.distributed as dist
+
+    steps, warmup = BATCH_LINE_STEPS, args.warmup
+    runs = {}
+    for name, split, gather in (("dp", "dp", "nccl"), ("tp_peer", "tp", "peer"), ("tp_nccl", "tp", "nccl")):
+        runs[name] = batch_run(split, gather, world, rank, device, steps, warmup)
+    tp3_value, tp3_tokens = config3_tp_run(world, rank, device, warmup)
+    gathers = gather_timing(world, device)
+    # dp tokens of every rank's sequences, in sequence order, onto every rank.
+    mine = torch.tensor(runs["dp"]["_tokens"], dtype=torch.int32, device=device)
+    every = torch.empty((world,) + tuple(mine.shape), dtype=torch.int32, device=device)
+    dist.all_gather_into_tensor(every, mine)
+    unsharded = every.reshape(-1, mine.shape[1]).cpu().tolist()
+    parity = {
+        "config4_tp_peer": runs["tp_peer"]["_tokens"] == unsharded,
+        "config4_tp_nccl": runs["tp_nccl"]["_tokens"] == unsharded,
+        "config3_tp_peer": tp3_tokens == replica_tokens if rank == 0 else None,
+    }
+    for r in runs.values():
+        r.pop("_tokens")
+    return {
+        "tp": {
+            "config4_peer": runs["tp_peer"], "config4_nccl": runs["tp_nccl"],
+            "config3_peer": {"decode_tokens_per_s": tp3_value, "steps": TP_STEPS,
+                             "note": "batch 1, per-operator kernels in one CUDA graph per step"},
+            "split": f"every linear's rows split over {world} GPUs, outputs all-gathered",
+        },
+        "dp": {"config4": runs["dp"], "split": f"{BATCH_SEQUENCES // world} sequences per GPU, full weights"},
+        "gather_us": gathers,
+        "tp_parity": all(v for v in parity.values() if v is not None),
+        "tp_parity_detail": parity,
+        "tp_parity_tokens": f"{BATCH_SEQUENCES} sequences x {steps + 1} tokens (config 4), {TP_TOKENS} tokens (config 3)",
+    }
 
 
 GEMV_COPIES = 32  # distinct config-0 weights per replay: 32 x 11.5 MB > L2
 
 
 def linear_rates(device, peak_gbs):
-    """Configs 0 and 2 as figures beside the headline step.
+    """Configs 0, 1 and 2 as figures beside the headline step.
 
     Config 0 (W8A8 GEMV, M=1, K=2048, N=5632, bias): GEMV_COPIES distinct
     seeded weights, one leafq_linear each with programmatic dependent launch
     (each launch streams its weights while the previous one finishes),
     captured in a CUDA graph and replayed; per-GEMV time = graph time /
     GEMV_COPIES.  The lm_head shape (N=32000) the same way with 4 copies.
+    Config 1 (INT4 weight-only GEMV, K=4096, N=11008, groups of 32): 8
+    distinct weights the same way.
     Config 2 (W8A8 prefill GEMM, M=512 tokens with 1% outliers x20,
     K=2048, N=5632 and K=5632, N=2048): 8 launches per graph on distinct
     weights, activation quantisation included."""
@@ -559,6 +740,26 @@ def linear_rates(device, peak_gbs):
                                "CUDA events"}
         del weights, ys
         torch.cuda.empty_cache()
+    # Config 1: INT4 weight-only GEMV (M=1, K=4096, N=11008, groups of 32,
+    # fp32 activations), 8 distinct weights of 28.2 MB (> L2).
+    rows, cols, group = 11008, 4096, 32
+    weights = []
+    for _ in range(8):
+        packed = torch.randint(0, 256, (rows, cols // 2), generator=gen, device=device, dtype=torch.uint8)
+        scales = torch.rand(rows, cols // group, generator=gen, device=device) * 1e-3 + 1e-4
+        weights.append(lq.QuantWeight(packed, scales, rows, cols, 4, group))
+    x = torch.randn(1, cols, generator=gen, device=device)
+    ys = [torch.empty(1, rows, device=device) for _ in weights]
+    us = timed([lambda w=w, y=y: lq.linear(x, w, activation_bits=32, out=y, flags=LEAFQ_FLAG_PDL)
+                for w, y in zip(weights, ys)])
+    nbytes = rows * cols // 2 + 4 * rows * (cols // group) + 4 * cols + 4 * rows  # W, scales, x, y
+    gbs = nbytes / (us * 1e-6) / 1e9
+    out["gemv_w4a32_config1"] = {"rows": rows, "cols": cols, "group": group, "us_per_call": us, "achieved": gbs,
+                                 "unit": "GB/s", "peak": peak_gbs, "frac": gbs / peak_gbs, "bytes_per_call": nbytes,
+                                 "method": "8 distinct weights (> L2) back to back with PDL in one CUDA graph, "
+                                           "CUDA events"}
+    del weights, ys
+    torch.cuda.empty_cache()
     peak_top = 2.0 * measured_bf16_tflops()
     tokens = 512
     xg = torch.randn(tokens, 5632, generator=gen, device=device)
@@ -582,17 +783,51 @@ def linear_rates(device, peak_gbs):
 
 
 BATCH_SEQUENCES, BATCH_PROMPT, BATCH_GENERATED = 64, 512, 256  # config 4
+BATCH_LINE_STEPS = 32  # config-4 decode steps timed beside the headline (N=1 line, and each split at N>1)
 
 
-def run_batch(args, rank, world, local_rank):
-    """Config 4: 64 requests of 512 random prompt ids, 256 greedy tokens
-    each, decoded together (``Decoder(sequences=...)``: one KV cache and
-    position per sequence, every linear over all sequences' rows).  With N
-    ranks the sequences are split over the GPUs (data parallel, full
-    weights per GPU).  One step = one decode token for every sequence; the
-    value is generated tokens/s over the whole job (prefill reported beside
-    it).  Every sequence's tokens equal the single-sequence decoder's and
-    the reference's (tests/test_gpu_decoder_batch.py)."""
+def _max_over_ranks(v, world, device):
+    import torch
+    import torch.distributed as dist
+
+    if world == 1:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def batch_prompts():
+    """Config 4's 64 seeded random 512-id prompts (identical on every rank)."""
+    import torch
+
+    from leaf_b200.stack import StackShape
+
+    gen = torch.Generator().manual_seed(7)
+    return torch.randint(0, StackShape().vocab, (BATCH_SEQUENCES, BATCH_PROMPT), generator=gen)
+
+
+def batch_run(split, gather, world, rank, device, steps, warmup, sampler_name=None):
+    """Config 4 on this rank's GPU: 64 requests of 512 random prompt ids,
+    greedy decode (``Decoder(sequences=...)``: one KV cache and position per
+    sequence, every linear over all sequences' rows).
+
+    split "dp": the sequences split over the ranks, full weights on each;
+    split "tp": every linear's rows split over the ranks (``Decoder(group=)``),
+    all sequences on every rank, each linear's output all-gathered (decode
+    steps by ``gather``: the library's peer-memory all-gather in the step's
+    CUDA graph, or NCCL; the prompt by NCCL).
+
+    Times the prefill and ``steps`` decode steps with CUDA events (max over
+    ranks), then runs ``generate_batch`` from host prompts to host tokens
+    (the end-to-end figure) and returns this rank's tokens [seqs][steps + 1]
+    for the parity check."""
     import torch
     import torch.distributed as dist
 
@@ -600,36 +835,21 @@ def run_batch(args, rank, world, local_rank):
     from leaf_b200.decoder import Decoder
     from leaf_b200.stack import RandomDecoderModel, StackShape
 
-    tp = args.batch_split == "tp" and world > 1
+    tp = split == "tp" and world > 1
     if BATCH_SEQUENCES % world:
         raise SystemExit(f"{BATCH_SEQUENCES} sequences do not split over {world} ranks")
     seqs = BATCH_SEQUENCES if tp else BATCH_SEQUENCES // world
-    steps = min(args.steps, BATCH_GENERATED - 1)
-    device = torch.device("cuda", local_rank)
-    torch.cuda.set_device(device)
+    steps = min(steps, BATCH_GENERATED - 1)
     shape = StackShape()
     model = RandomDecoderModel(shape, seed=1234, device=device)
     dec = Decoder(model, device=device, sequences=seqs, capacity=BATCH_PROMPT + BATCH_GENERATED,
-                  group=dist.group.WORLD if tp else None, gather=args.tp_gather)
+                  group=dist.group.WORLD if tp else None, gather=gather)
     model.release()
     del model
     lib = lq.load()
     stream = torch.cuda.current_stream(device)
-    gen = torch.Generator().manual_seed(7)
-    every = torch.randint(0, shape.vocab, (BATCH_SEQUENCES, BATCH_PROMPT), generator=gen)
+    every = batch_prompts()
     prompts = every.tolist() if tp else every[rank * seqs:(rank + 1) * seqs].tolist()
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    def max_over_ranks(v):
-        if world == 1:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
     dec.capture_decode()
 
     def prefill():
@@ -639,17 +859,14 @@ def run_batch(args, rank, world, local_rank):
                                        dec._bufs(1)["ids"].data_ptr()))
 
     prefill()
-    for _ in range(max(args.warmup, 3)):
+    for _ in range(max(warmup, 3)):
         dec._decode_step()
     torch.cuda.synchronize(device)
-    out_dir = REPO / "gpurun_out"
-    out_dir.mkdir(exist_ok=True)
-    visible = [v for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
-    smi_id = visible[local_rank] if local_rank < len(visible) else str(device.index)
-    sampler = ClockSampler(smi_id, out_dir / f"clocks_batch_rank{rank}.csv")
-    time.sleep(0.3)
-    # Prefill (timed on its own), then `steps` decode steps from position 512.
-    barrier()
+    sampler = None
+    if sampler_name:
+        sampler = ClockSampler(smi_index(device.index, device), sampler_name)
+        time.sleep(0.3)
+    _barrier(world)
     torch.cuda.synchronize(device)
     p0, p1, d1 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
     p0.record(stream)
@@ -659,94 +876,119 @@ def run_batch(args, rank, world, local_rank):
         dec._decode_step()
     d1.record(stream)
     torch.cuda.synchronize(device)
-    barrier()
-    prefill_ms = max_over_ranks(p0.elapsed_time(p1))
-    decode_ms = max_over_ranks(p1.elapsed_time(d1))
+    _barrier(world)
+    prefill_ms = _max_over_ranks(p0.elapsed_time(p1), world, device)
+    decode_ms = _max_over_ranks(p1.elapsed_time(d1), world, device)
     # End to end through the public API: generate_batch from host prompts to
     # host tokens (prompt upload, prefill, every decode step, tokens back).
-    barrier()
+    _barrier(world)
     torch.cuda.synchronize(device)
     t0 = time.perf_counter()
     dec.reset()
     tokens = dec.generate_batch(prompts, steps + 1)
     torch.cuda.synchronize(device)
-    e2e_s = max_over_ranks(time.perf_counter() - t0)
-    barrier()
-    time.sleep(0.2)
-    clocks = sampler.stop()
+    e2e_s = _max_over_ranks(time.perf_counter() - t0, world, device)
+    _barrier(world)
+    clocks = None
+    if sampler is not None:
+        time.sleep(0.2)
+        clocks = sampler.stop()
     status = lib.leafq_device_status()
     if status != 0:
         raise RuntimeError(f"device status {status}: {lib.leafq_last_error().decode()}")
     assert all(len(t) == steps + 1 for t in tokens)
     dec.close()
-
-    value = BATCH_SEQUENCES * steps / (decode_ms * 1e-3)
-    if rank == 0:
-        peak, peak_kind = measured_peaks()
-        h, kv, d, layers = shape.hidden, shape.kv_heads, shape.hidden // shape.heads, shape.layers
-        weight_bytes = (shape.weight_bytes() + shape.scale_bytes()) / (world if tp else 1)
-        mean_keys = BATCH_PROMPT + (steps + 1) / 2
-        kv_bytes = layers * seqs * 2 * kv * d * 4 * mean_keys
-        step_bytes = weight_bytes + kv_bytes
-        ms_step = decode_ms / steps
-        achieved = step_bytes / (ms_step * 1e-3) / 1e9
-        cpu = None
-        if world == 1 and not args.no_cpu_baseline:
-            threads = max(1, min(os.cpu_count() or 1, 64))
-            try:
-                cpu_value, sample = cpu_reference_decoder(threads, 9, prompt=BATCH_PROMPT)
-                cpu = {"value": cpu_value, "unit": UNIT, "cores": threads, "kind": "reference",
-                       "sample": sample + "; the reference serves the 64 requests one after another, so "
-                                          "this is its config-4 throughput"}
-            except Exception as exc:  # noqa: BLE001
-                cpu = {"value": None, "unit": UNIT, "cores": threads, "kind": "reference",
-                       "sample": f"failed: {exc}"}
-        line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps,
-            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {
-                "workload": f"config 4: tinyllama-1.1b w8a8, {BATCH_SEQUENCES} sequences x {BATCH_PROMPT}-token "
-                            f"random prompts, greedy decode (one step = one token for every sequence), "
-                            f"positions {BATCH_PROMPT}..{BATCH_PROMPT + steps - 1}",
-                "model": "TinyLlama-1.1B shape (random-init INT8 per-row weights)",
-                "global_batch": BATCH_SEQUENCES, "seq_len": BATCH_PROMPT + BATCH_GENERATED,
-                "parallelism": (f"tp{world} (every linear's rows split over the GPUs, each output "
-                                f"all-gathered: decode steps by {args.tp_gather}, the prompt by NCCL; all "
-                                f"{seqs} sequences on every GPU)") if tp else
-                               f"dp{world} ({seqs} sequences per GPU, full weights each)",
-                "l2": "inputs larger than L2 (1.04 GB of weights and the KV caches streamed per step)",
-            },
-            "prefill": {"ms": prefill_ms, "tokens_per_s": BATCH_SEQUENCES * BATCH_PROMPT / (prefill_ms * 1e-3)},
-            "roofline": {
-                "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                "traffic": None, "kernel": "whole decode step (per-operator kernels in one CUDA graph)",
-                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
-                "algorithmic_bytes_per_step": step_bytes,
-            },
-            "e2e": {"value": BATCH_SEQUENCES * (steps + 1) / e2e_s, "unit": UNIT,
-                    "h2d_bytes_per_step": int(seqs * BATCH_PROMPT * 4 / (steps + 1)),
-                    "d2h_bytes_per_step": int(seqs * 4),
-                    "note": "generate_batch wall time including the prompt prefill"},
-            "clocks": clocks,
-            "cpu_baseline": cpu,
-            "when": datetime.datetime.now(datetime.timezone.utc).isoformat(timespec="seconds"),
-        }
-        print(json.dumps(line), flush=True)
+    del dec
+    torch.cuda.empty_cache()
+    h, kv, d, layers = shape.hidden, shape.kv_heads, shape.hidden // shape.heads, shape.layers
+    weight_bytes = (shape.weight_bytes() + shape.scale_bytes()) / (world if tp else 1)
+    mean_keys = BATCH_PROMPT + (steps + 1) / 2
+    step_bytes = weight_bytes + layers * seqs * 2 * kv * d * 4 * mean_keys
+    ms_step = decode_ms / steps
+    return {
+        "decode_tokens_per_s": BATCH_SEQUENCES * steps / (decode_ms * 1e-3),
+        "ms_per_step": ms_step, "steps": steps,
+        "prefill": {"ms": prefill_ms, "tokens_per_s": BATCH_SEQUENCES * BATCH_PROMPT / (prefill_ms * 1e-3)},
+        "e2e_tokens_per_s": BATCH_SEQUENCES * (steps + 1) / e2e_s,
+        "hbm_gbs_per_gpu": step_bytes / (ms_step * 1e-3) / 1e9,
+        "algorithmic_bytes_per_step_per_gpu": step_bytes,
+        "sequences_per_gpu": seqs,
+        "clocks": clocks,
+        "_tokens": tokens,
+    }
 
 
-def read_traffic():
-    """DRAM bytes per decode step from the committed ncu summary, if any."""
-    path = REPO / "profiles" / "decode_model_tinyllama_step.md"
-    if not path.exists():
-        return None
-    for line in path.read_text().splitlines():
-        if line.startswith("traffic_bytes_per_step:"):
-            try:
-                return float(line.split(":", 1)[1].strip())
-            except ValueError:
-                return None
-    return None
+def run_batch(args, rank, world, local_rank):
+    """Config 4 as the bench line (--workload batch): 64 requests of 512
+    random prompt ids, greedy decode; one step = one decode token for every
+    sequence; value = generated tokens/s over the whole job (prefill beside
+    it).  With N ranks the sequences are split over the GPUs (dp) or every
+    linear's rows are (tp).  Every sequence's tokens equal the
+    single-sequence decoder's and the reference's
+    (tests/test_gpu_decoder_batch.py)."""
+    import torch
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    tp = args.batch_split == "tp" and world > 1
+    r = batch_run(args.batch_split, args.tp_gather, world, rank, device, args.steps, args.warmup,
+                  sampler_name=f"clocks_batch_rank{rank}.csv")
+    if rank != 0:
+        return
+    peak, peak_kind = measured_peaks()
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        threads = max(1, min(os.cpu_count() or 1, 64))
+        try:
+            cpu_value, sample = cpu_reference_decoder(threads, 9, prompt=BATCH_PROMPT)
+            cpu = {"value": cpu_value, "unit": UNIT, "cores": threads, "kind": "reference",
+                   "sample": sample + "; the reference serves the 64 requests one after another, so "
+                                      "this is its config-4 throughput"}
+        except Exception as exc:  # noqa: BLE001
+            cpu = {"value": None, "unit": UNIT, "cores": threads, "kind": "reference",
+                   "sample": f"failed: {exc}"}
+    seqs = r["sequences_per_gpu"]
+    steps = r["steps"]
+    line = {
+        "metric": METRIC, "value": r["decode_tokens_per_s"], "unit": UNIT, "n_gpus": world, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {
+            "workload": f"config 4: tinyllama-1.1b w8a8, {BATCH_SEQUENCES} sequences x {BATCH_PROMPT}-token "
+                        f"random prompts, greedy decode (one step = one token for every sequence), "
+                        f"positions {BATCH_PROMPT}..{BATCH_PROMPT + steps - 1}",
+            "model": "TinyLlama-1.1B shape (random-init INT8 per-row weights)",
+            "global_batch": BATCH_SEQUENCES, "seq_len": BATCH_PROMPT + BATCH_GENERATED,
+            "parallelism": (f"tp{world} (every linear's rows split over the GPUs, each output "
+                            f"all-gathered: decode steps by {args.tp_gather}, the prompt by NCCL; all "
+                            f"{seqs} sequences on every GPU)") if tp else
+                           f"dp{world} ({seqs} sequences per GPU, full weights each)",
+            "l2": "inputs larger than L2 (1.04 GB of weights and the KV caches streamed per step)",
+        },
+        "prefill": r["prefill"],
+        "roofline": {
+            "bound": "hbm", "achieved": r["hbm_gbs_per_gpu"], "peak": peak, "unit": "GB/s",
+            "frac": r["hbm_gbs_per_gpu"] / peak, "traffic": None,
+            "kernel": "whole decode step (per-operator kernels in one CUDA graph)",
+            "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+            "algorithmic_bytes_per_step": r["algorithmic_bytes_per_step_per_gpu"],
+        },
+        "e2e": {"value": r["e2e_tokens_per_s"], "unit": UNIT,
+                "h2d_bytes_per_step": int(seqs * BATCH_PROMPT * 4 / (steps + 1)),
+                "d2h_bytes_per_step": int(seqs * 4),
+                "note": "generate_batch wall time including the prompt prefill"},
+        "clocks": r["clocks"],
+        "cpu_baseline": cpu,
+        "when": datetime.datetime.now(datetime.timezone.utc).isoformat(timespec="seconds"),
+    }
+    print(json.dumps(line), flush=True)
+
+
+# DRAM traffic of decode_model_kernel per algorithmic byte: dram__bytes_read.sum +
+# dram__bytes_write.sum over decoder_step_bytes, from the ncu capture of
+# `bench.py --case model_small` (3 layers at full width; traffic grows with the
+# weights streamed, each read once, so the ratio carries to the 22-layer step).
+DECODE_TRAFFIC_RATIO = 1.019
 
 
 def main():

@@ -61,6 +61,15 @@ int leafq_version(void);
  * give up.  Synchronises the current device.  LEAFQ_OK or LEAFQ_ERR_TIMEOUT. */
 int leafq_device_status(void);
 
+/* How long a device-side wait (a pipeline barrier, a hand-off word another
+ * block or rank writes) spins before it gives up, records the failure for
+ * leafq_device_status() and lets its kernel return: 2 s by default (0
+ * restores it), 1 us .. 60 s otherwise.  Applies to the current device;
+ * synchronises it first.  The reference's counterpart is its bounded worker
+ * spin (engine/include/leaf/runtime/host_support.h:185-197); a short limit
+ * lets a test make a wait run out without hanging anything. */
+int leafq_set_wait_limit_ns(uint64_t nanoseconds);
+
 /* Per-token dynamic activation quantisation.
  * Replaces decoder.cpp:1028-1044 (scale = max(absmax / 127, 1e-12), codes =
  * round-half-even(x * (1 / scale)) as quantize_input_avx, :618-627).  q is
@@ -184,19 +193,21 @@ int leafq_decode_plan_create(const leafq_decode_op* ops, int nops, int tokens,
 int leafq_decode_plan_run(void* stream, leafq_decode_plan_t* plan);
 int leafq_decode_plan_destroy(leafq_decode_plan_t* plan);
 
-/* Per-row W8A8 linear (INT8 weights, group == cols, cols a multiple of 16
- * and >= 128) that allocates nothing: for callers that cannot allocate
- * device memory -- a plugin whose host runtime owns all device memory, a
- * serving loop that may not touch the allocator after start-up, an embedder
- * with a fixed budget -- and so cannot hand leafq_linear a workspace.  No
- * counterpart in the reference (its CPU decoder reuses host vectors).
- * Same results as leafq_linear for the same inputs.  Its scratch is a
- * library-owned device array of 8 MiB of codes plus 16384 token scales,
- * held on every GPU that loads the library until exit: calls with
- * tokens * cols > 8 MiB or tokens > 16384 return LEAFQ_ERR_INVALID.  The
- * first call on a device looks up the array's address (make it before any
- * stream capture).  All calls share the array: calls that overlap on the
- * GPU race; calls ordered on one stream do not. */
+/* Per-row W8A8 linear (INT8 weights, group == cols) that allocates nothing:
+ * for callers that cannot allocate device memory -- a plugin whose host
+ * runtime owns all device memory, a serving loop that may not touch the
+ * allocator after start-up, an embedder with a fixed budget -- and so cannot
+ * hand leafq_linear a workspace.  No counterpart in the reference (its CPU
+ * decoder reuses host vectors).  It runs the kernels leafq_linear runs for
+ * the same call (the decode GEMV for 1-8 tokens needs no scratch), so the
+ * results are leafq_linear's bit for bit.  Its scratch is a library-owned
+ * device array of 8 MiB of codes plus 16384 token scales, held on every GPU
+ * that loads the library until exit: calls with tokens * cols > 8 MiB or
+ * tokens > 16384 return LEAFQ_ERR_INVALID.  The first call in each CUDA
+ * context looks up the array's address (make it before any stream capture;
+ * after a device reset the next call looks it up again).  All calls share
+ * the array: calls that overlap on the GPU race; calls ordered on one stream
+ * do not. */
 int leafq_linear_w8a8_static_scratch(void* stream, const float* x, int64_t tokens, int64_t cols,
                                      const int8_t* weight, const float* weight_scales,
                                      int64_t rows, const float* bias, float* y, uint32_t flags);

@@ -36,6 +36,7 @@ _SIGNATURES = {
     "leafq_last_error": ([], ctypes.c_char_p),
     "leafq_version": ([], _int),
     "leafq_device_status": ([], _int),
+    "leafq_set_wait_limit_ns": ([ctypes.c_uint64], _int),
     "leafq_quantize_act": ([_vp, _vp, _i64, _i64, _vp, _vp], _int),
     "leafq_linear_workspace_bytes": ([_i64, _i64, _int, _i64, _int], _size),
     "leafq_linear": ([_vp, _vp, _i64, _i64, _vp, _vp, _i64, _int, _i64, _int, _vp, _vp, _vp, _size,

@@ -23,6 +23,7 @@
 namespace leafq {
 
 __device__ unsigned int g_device_error = 0;
+__device__ unsigned long long g_wait_limit_ns = kDefaultWaitLimitNs;
 
 namespace {
 thread_local std::string t_error;
@@ -87,6 +88,17 @@ int check_weight(int64_t tokens, int64_t cols, int64_t rows, int bits, int64_t g
 
 }  // namespace
 
+bool integer_path_takes_gemv(int64_t tokens, int64_t cols, int bits, int64_t group, const void* weight,
+                             const float* x) {
+    return integer_path_uses_gemv(tokens, cols, bits, group) &&
+           gemv_w8a8_supported(tokens, cols, bits, group, weight, x);
+}
+
+bool integer_path_takes_gemm_tc(int64_t tokens, int64_t cols, int64_t rows, int bits, int64_t group,
+                                const void* weight) {
+    return tokens > kGemvMaxTokens && gemm_tc_supported(tokens, cols, rows, bits, group, weight);
+}
+
 void set_error(const std::string& message) { t_error = message; }
 void clear_error() { t_error.clear(); }
 
@@ -148,6 +160,20 @@ int leafq_device_status(void) {
     set_error("a device wait timed out (site " + std::to_string(word >> 16) + ", block " +
               std::to_string(word & 0xffffu) + ")");
     return LEAFQ_ERR_TIMEOUT;
+}
+
+int leafq_set_wait_limit_ns(uint64_t nanoseconds) {
+    clear_error();
+    const unsigned long long limit = nanoseconds == 0 ? kDefaultWaitLimitNs : nanoseconds;
+    if (limit < 1000ull || limit > 60000000000ull) {
+        set_error("leafq_set_wait_limit_ns: the limit must be 0 (default, 2 s) or 1 us .. 60 s");
+        return LEAFQ_ERR_INVALID;
+    }
+    // Finish the kernels in flight first, so none sees the limit change in
+    // the middle of a wait.
+    cudaError_t err = cudaDeviceSynchronize();
+    if (err == cudaSuccess) err = cudaMemcpyToSymbol(g_wait_limit_ns, &limit, sizeof(limit));
+    return cuda_status(err, "leafq_set_wait_limit_ns");
 }
 
 int leafq_quantize_act(void* stream, const float* x, int64_t tokens, int64_t cols, int8_t* q,

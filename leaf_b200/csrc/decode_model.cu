@@ -129,7 +129,7 @@ __device__ __forceinline__ bool wait_tagged(const uint64_t* p, uint32_t tag, flo
         for (uint32_t spins = 1;; ++spins) {
             w = load_tagged(p);
             if (static_cast<uint32_t>(w >> 32) == tag) break;
-            if ((spins & 31u) == 0u && (device_error_raised() || global_timer_ns() - start > kWaitLimitNs)) {
+            if ((spins & 31u) == 0u && (device_error_raised() || global_timer_ns() - start > wait_limit_ns())) {
                 record_device_error(kSiteDecodeDependency);
                 value = 0.0f;
                 return false;
@@ -182,7 +182,7 @@ __device__ __forceinline__ bool load_tagged_x(const uint64_t* x, int64_t vecs, u
                     load_tagged2(x + 4 * i + 2, w[k][2], w[k][3]);
                     if (all_tagged()) break;
                     if ((spins & 31u) == 0u &&
-                        (device_error_raised() || global_timer_ns() - start > kWaitLimitNs)) {
+                        (device_error_raised() || global_timer_ns() - start > wait_limit_ns())) {
                         record_device_error(kSiteDecodeDependency);
                         good = false;
                         break;

@@ -276,7 +276,7 @@ decode_persistent_kernel(const Op* __restrict__ ops_global, int nops, uint32_t* 
                                 (uint32_t)(c >> 32) == tag && (uint32_t)(d >> 32) == tag)
                                 break;
                             if ((spins & 31u) == 0u &&
-                                (device_error_raised() || global_timer_ns() - start > kWaitLimitNs)) {
+                                (device_error_raised() || global_timer_ns() - start > wait_limit_ns())) {
                                 record_device_error(kSiteDecodeDependency);
                                 ok = false;
                                 *abort_flag = 1;

@@ -26,10 +26,15 @@ namespace leafq {
 // Codes: 0 = fine; otherwise (site << 16) | (blockIdx.x & 0xffff).
 extern __device__ unsigned int g_device_error;
 
-// A wait gives up after this many nanoseconds of %globaltimer (2 s): far
-// longer than any legitimate wait in these kernels, short enough that a
-// broken pipeline ends on its own.
-constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+// A wait gives up after g_wait_limit_ns nanoseconds of %globaltimer: by
+// default 2 s, far longer than any legitimate wait in these kernels, short
+// enough that a broken pipeline ends on its own.  The host can change it
+// per device (leafq_set_wait_limit_ns), e.g. to drive a wait to its limit
+// in a test.
+constexpr unsigned long long kDefaultWaitLimitNs = 2000000000ull;
+extern __device__ unsigned long long g_wait_limit_ns;
+
+__device__ __forceinline__ unsigned long long wait_limit_ns() { return g_wait_limit_ns; }
 
 enum WaitSite : unsigned {
     kSiteGemvFull = 1,
@@ -119,7 +124,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
         if (mbar_try_wait(bar, parity)) return true;
         if ((spins & 255u) == 0u) {
             if (device_error_raised()) return false;
-            if (global_timer_ns() - start > kWaitLimitNs) {
+            if (global_timer_ns() - start > wait_limit_ns()) {
                 record_device_error(site);
                 return false;
             }

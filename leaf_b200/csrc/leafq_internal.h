@@ -82,6 +82,15 @@ int launch_gemv_w8a8(cudaStream_t s, const float* x, int64_t tokens, int64_t col
                      const int8_t* weight, const float* wscales, int64_t rows, const float* bias,
                      float* y, bool pdl, const PeerStore* peer = nullptr);
 
+// The path leafq_linear takes for an integer call (activation bits 8): the
+// fused-quantisation GEMV (no workspace), else codes into a workspace and
+// then the tcgen05 GEMM when integer_path_takes_gemm_tc, else the generic
+// integer kernel.
+bool integer_path_takes_gemv(int64_t tokens, int64_t cols, int bits, int64_t group, const void* weight,
+                             const float* x);
+bool integer_path_takes_gemm_tc(int64_t tokens, int64_t cols, int64_t rows, int bits, int64_t group,
+                                const void* weight);
+
 // Generic integer linear from codes (any group, bits 8 / 4, any tokens).
 int launch_linear_int_q(cudaStream_t s, const int8_t* q, const float* sx, int64_t tokens,
                         int64_t cols, const void* weight, const float* wscales, int64_t rows,

@@ -74,7 +74,7 @@ __global__ void __launch_bounds__(kThreads) allgather_collect_kernel(
         while (true) {
             asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(w) : "l"(base + i) : "memory");
             if (static_cast<uint32_t>(w >> 32) == tag) break;
-            if (gave_up || global_timer_ns() - start > kWaitLimitNs) {
+            if (gave_up || global_timer_ns() - start > wait_limit_ns()) {
                 if (!gave_up) record_device_error(kSiteAllGather);
                 gave_up = true;
                 w = 0x7fc00000ull;  // NaN: a peer never stored this word

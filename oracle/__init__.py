@@ -38,12 +38,26 @@ _lib = None
 _ref = None
 
 
+def reference_root():
+    """The reference checkout the ``_ref`` recipe compiles from: the
+    LEAF_REFERENCE environment variable, else a ``reference`` directory beside
+    this repository; None when neither holds the engine sources."""
+    env = os.environ.get("LEAF_REFERENCE")
+    for root in ([Path(env)] if env else []) + [HERE.parent.parent / "reference"]:
+        if (root / "engine" / "src" / "decoder.cpp").exists():
+            return root
+    return None
+
+
 def build(ref: bool = False) -> None:
     """Compile the C restatement (and, when the reference tree is present, the
     reference kernels)."""
     subprocess.run(["make", "-s", "-C", str(HERE), "oracle"], check=True)
     if ref:
-        subprocess.run(["make", "-s", "-C", str(HERE), "ref"], check=True)
+        root = reference_root()
+        if root is None:
+            raise FileNotFoundError("no reference tree: set LEAF_REFERENCE")
+        subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF={root}"], check=True)
 
 
 def lib() -> ctypes.CDLL:

@@ -1,5 +1,6 @@
 """Golden decoder outputs from the reference itself (run where the reference
-tree is available: REF, default /root/reference; needs ``make -C oracle ref``).
+tree is available: LEAF_REFERENCE, or a ``reference`` directory beside this
+repository; needs the oracle/_ref build).
 
 For each fixture model of decoder_fixture.py:
   1. write the seeded weights as a Hugging Face snapshot and export it with the
@@ -33,7 +34,10 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parents[1]
-REF = Path(os.environ.get("REF", "/root/reference"))
+sys.path.insert(0, str(REPO))
+import oracle as _oracle  # noqa: E402
+
+REF = _oracle.reference_root() or Path(os.environ.get("LEAF_REFERENCE", "reference"))
 sys.path.insert(0, str(HERE))
 sys.path.insert(0, str(REPO))
 

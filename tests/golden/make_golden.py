@@ -1,7 +1,8 @@
 """Generate the golden vectors in this directory from the reference itself.
 
-Run in a checkout where the reference tree is available (REF, default
-/root/reference) and the reference kernels are built (``make -C oracle ref``):
+Run in a checkout where the reference tree is available (LEAF_REFERENCE, or a
+``reference`` directory beside this repository) and the reference kernels are
+built (oracle.build(ref=True)):
 
     python tests/golden/make_golden.py
 
@@ -23,7 +24,10 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parents[1]
-REF = Path(os.environ.get("REF", "/root/reference"))
+sys.path.insert(0, str(REPO))
+import oracle as _oracle  # noqa: E402
+
+REF = _oracle.reference_root() or Path(os.environ.get("LEAF_REFERENCE", "reference"))
 sys.path.insert(0, str(REPO))
 sys.path.insert(0, str(REF))
 
