@@ -778,6 +778,20 @@ def linear_rates(device, peak_gbs):
                                           "method": "8 distinct weights back to back in one CUDA graph "
                                                     "(activation quantisation included)"}
         del wl, yl
+    # The graph executor's INT8 GEMM (gemm_i8_per_channel) at the config-2
+    # shape with its weight as the graph stores it, [k, n] (read MN-major by
+    # the tensor cores): 8 distinct weights, codes given.
+    m, k, n = 512, 2048, 5632
+    codes = torch.randint(-127, 128, (m, k), generator=gen, device=device, dtype=torch.int8)
+    bl = [torch.randint(-127, 128, (k, n), generator=gen, device=device, dtype=torch.int8) for _ in range(8)]
+    sc = torch.rand(n, generator=gen, device=device) * 0.01
+    us = timed([lambda b=b: lq.gemm_i8_per_channel(codes, b, None, 0.01, sc) for b in bl])
+    tops = 2.0 * m * n * k / (us * 1e-6) / 1e12
+    out["graph_gemm_i8_per_channel_m512_k2048_n5632"] = {
+        "us_per_call": us, "achieved": tops, "unit": "TOP/s", "peak": peak_top, "frac": tops / peak_top,
+        "peak_source": "2 x measured bf16 burst (no INT8 figure measured)",
+        "method": "8 distinct [k, n] weights back to back in one CUDA graph (codes given, output allocated per call)"}
+    del bl
     torch.cuda.empty_cache()
     return out
 

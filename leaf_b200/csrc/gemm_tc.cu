@@ -268,7 +268,15 @@ gemm_w8a8_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
     }
 }
 
+// 2-D int8 map over a row-major [outer, inner] matrix, box [box_outer, 128].
+int make_map(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, int box_outer) {
+    return make_tma_map_u8(map, base, inner, outer, BK, box_outer);
+}
+
+}  // namespace
+
 // ------------------------------------------------------------ tensor maps
+namespace {
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
@@ -287,9 +295,10 @@ EncodeTiledFn encode_fn() {
     });
     return fn;
 }
+}  // namespace
 
-// 2-D int8 map over a row-major [outer, inner] matrix, box [box_outer, 128].
-int make_map(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, int box_outer) {
+int make_tma_map_u8(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, int box_inner,
+                    int box_outer) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) {
         set_error("cuTensorMapEncodeTiled is not available from the driver");
@@ -297,7 +306,7 @@ int make_map(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, i
     }
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(inner)};
-    const cuuint32_t box[2] = {BK, static_cast<cuuint32_t>(box_outer)};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(box_outer)};
     const cuuint32_t estrides[2] = {1, 1};
     const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
                           box, estrides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -308,8 +317,6 @@ int make_map(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, i
     }
     return LEAFQ_OK;
 }
-
-}  // namespace
 
 bool gemm_tc_supported(int64_t tokens, int64_t cols, int64_t rows, int bits, int64_t group,
                        const void* weight) {

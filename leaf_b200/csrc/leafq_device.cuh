@@ -300,6 +300,32 @@ __host__ __device__ constexpr uint32_t umma_idesc_i8(uint32_t m, uint32_t n) {
     return (2u << 4) | (1u << 7) | (1u << 10) | ((n >> 3) << 17) | ((m >> 4) << 24);
 }
 
+// 2-D tensor map over a row-major uint8 [outer, inner] matrix (inner
+// contiguous, a multiple of 16 bytes) with 128-byte swizzle and box
+// [box_outer, box_inner]; out-of-range elements load as zero.  Host side.
+int make_tma_map_u8(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, int box_inner,
+                    int box_outer);
+
+// Instruction descriptor for kind::i8 with the B operand MN-major (bit 16):
+// B tiles hold rows of N contiguous, as a [k, n] matrix is stored.
+__host__ __device__ constexpr uint32_t umma_idesc_i8_bmn(uint32_t m, uint32_t n) {
+    return umma_idesc_i8(m, n) | (1u << 16);
+}
+
+// Shared-memory descriptor for an MN-major operand tile written by TMA with
+// 128-byte swizzle in boxes of [rows of K, 128 bytes of N]: 8-row K groups
+// 1024 bytes apart (stride byte offset), 128-column N blocks `lbo` bytes
+// apart (leading byte offset), layout type 2.
+__device__ __forceinline__ uint64_t umma_desc_mn_sw128(uint32_t smem_addr, uint32_t lbo) {
+    uint64_t desc = 0;
+    desc |= static_cast<uint64_t>((smem_addr >> 4) & 0x3fffu);
+    desc |= static_cast<uint64_t>((lbo >> 4) & 0x3fffu) << 16;
+    desc |= static_cast<uint64_t>(1024u >> 4) << 32;
+    desc |= static_cast<uint64_t>(1u) << 46;
+    desc |= static_cast<uint64_t>(2u) << 61;
+    return desc;
+}
+
 // ------------------------------------------------ peer-memory all-gather
 // One flag-in-data word {value, tag} of gathered element (token, local_row),
 // stored into every rank's receive buffer.  The 8-byte store is single-copy
