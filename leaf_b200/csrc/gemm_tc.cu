@@ -9,10 +9,13 @@
 //   y = fma(float(acc) * sx[token], sw[row], 0.0f) + (bias[row] or 0.0f).
 //
 // Tiling: D[128 tokens, BN rows] per tile (one UMMA of M=128, N=BN, K=32
-// per instruction, four per 128-byte K block); BN = 256 or 128 when their
+// per instruction, four per 128-byte K block).  More than 64 tokens: BN of
+// 256, 160, 128, 64 or 32, whichever needs the fewest rounds of tiles x
+// width (so M=512 x N=5632 runs one round of 144 tiles 160 wide).  At most
+// 64 tokens (prefill chunks, batched decode of a few dozen sequences, where
+// the weight stream must come through most SMs): 256 or 128 when their
 // tiles give every SM one, else 64 when its tiles cover about 4/5 of the
-// SMs, else 32 (few tokens: prefill chunks, batched decode of a few dozen
-// sequences, where the weight stream must come through most SMs).  Operands are K-major: the
+// SMs, else 32.  Operands are K-major: the
 // codes [tokens, cols] and the weights [rows, cols] are both row-major with
 // K contiguous, loaded by TMA with 128-byte swizzle into a ring of 4 to 10
 // stages (about 200 KB); with at most 64 tokens the code box is cut to 32 or
@@ -51,9 +54,10 @@ struct TileCfg {
     static constexpr int kBBytes = BN * BK;
     // As many 128-byte K stages as fit in ~200 KB of shared memory.
     static constexpr int kStages = kThin ? (196608 / (kAStage + kBBytes) < 16 ? 196608 / (kAStage + kBBytes) : 16)
-                                         : (BN == 256 ? 4 : BN == 128 ? 6 : BN == 64 ? 8 : 10);
+                                         : (BN == 256 ? 4 : BN == 160 ? 5 : BN == 128 ? 6 : BN == 64 ? 8 : 10);
     static constexpr int kAccCols = BN;  // TMEM columns per accumulator
-    static constexpr int kTmemCols = 2 * kAccCols;
+    // Allocated TMEM columns: a power of two covering both accumulators.
+    static constexpr int kTmemCols = 2 * kAccCols <= 64 ? 64 : 2 * kAccCols <= 128 ? 128 : 2 * kAccCols <= 256 ? 256 : 512;
     static constexpr size_t kColBytes = 4 * 2 * 2 * BN * sizeof(float);  // [warp][acc][scale | bias][BN]
     static constexpr size_t kSmemBytes =
         (size_t)kStages * (kAStage + kBBytes) + 1024 /*barriers*/ + kColBytes + 1024 /*align*/;
@@ -376,10 +380,29 @@ int launch_gemm_tc(cudaStream_t s, const int8_t* q, const float* sx, int64_t tok
         if (tiles(64) * 5 >= sms * 4) return run_tiles<64, true>(s, q, weight, cols, tokens, rows, a, pdl);
         return run_tiles<32, true>(s, q, weight, cols, tokens, rows, a, pdl);
     }
-    if (tiles(256) >= sms) return run_tiles<256, false>(s, q, weight, cols, tokens, rows, a, pdl);
-    if (tiles(128) >= sms) return run_tiles<128, false>(s, q, weight, cols, tokens, rows, a, pdl);
-    if (tiles(64) * 5 >= sms * 4) return run_tiles<64, false>(s, q, weight, cols, tokens, rows, a, pdl);
-    return run_tiles<32, false>(s, q, weight, cols, tokens, rows, a, pdl);
+    // More tokens: the width with the least work per SM, counted as rounds of
+    // tiles x (width + 32) -- a partial last round costs a whole one, and each
+    // tile carries a fixed prologue / epilogue of about 32 columns' worth; the
+    // wider on a tie.  M=512 x N=5632 takes 160 (144 tiles, one round) rather
+    // than 128 (176 tiles: a second round 19 % full); large M keeps 256.
+    const int widths[5] = {256, 160, 128, 64, 32};
+    int best = 256;
+    int64_t best_cost = -1;
+    for (int bn : widths) {
+        const int64_t rounds = (tiles(bn) + sms - 1) / sms;
+        const int64_t cost = rounds * (bn + 32);
+        if (best_cost < 0 || cost < best_cost) {
+            best = bn;
+            best_cost = cost;
+        }
+    }
+    switch (best) {
+        case 256: return run_tiles<256, false>(s, q, weight, cols, tokens, rows, a, pdl);
+        case 160: return run_tiles<160, false>(s, q, weight, cols, tokens, rows, a, pdl);
+        case 128: return run_tiles<128, false>(s, q, weight, cols, tokens, rows, a, pdl);
+        case 64: return run_tiles<64, false>(s, q, weight, cols, tokens, rows, a, pdl);
+        default: return run_tiles<32, false>(s, q, weight, cols, tokens, rows, a, pdl);
+    }
 }
 
 }  // namespace leafq

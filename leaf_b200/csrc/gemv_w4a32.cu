@@ -8,7 +8,10 @@
 // (h1 + h3) (reduce(), :294-298) and adds partial * scale to the row sum
 // with one FMA, group after group (GCC fuses :386).
 //
-// Layout of one block (one per SM): a producer warp streams stages of 16
+// Groups of 32 columns run gemv_w4a32_g32_kernel below (16 compute warps,
+// packed f32x2 arithmetic, a walker warp overlapping the ordered group
+// chains with the next stage).  Other group sizes run gemv_w4a32_kernel:
+// one block per SM, a producer warp streams stages of 16
 // rows -- the packed weights (cols / 2 bytes per row) and their group
 // scales -- with 1-D bulk copies.  Each of the 256 consumer threads owns one
 // group index g (and a row slot when a row has fewer than 256 groups) and
@@ -172,11 +175,204 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_w4a32_kernel(const W4Args a)
             float result = 0.0f;
             const float* pr = P + tid * (G + 1);
             const float* sr = SC + tid * (G + 1);
+#pragma unroll 16
             for (int k = 0; k < G; ++k) result = __fmaf_rn(pr[k], sr[k], result);
             const int64_t row = r0 + tid;
             a.y[row] = __fadd_rn(result, a.bias ? __ldg(a.bias + row) : 0.0f);
         }
         consumer_sync();
+    }
+}
+
+// ------------------------------------------------------------------------
+// Groups of 32 columns (the reference's default INT4 export, config 1): one
+// 32-column block per group, so every accumulator lane is one product
+// fma(w, x, 0).  18 warps: 16 compute warps, a walker warp and the producer.
+// Compute thread (g, slot) keeps group g's 32 x values in registers as 16
+// packed pairs and computes the group partial of rows slot, slot + slots, ...
+// of each stage with packed f32x2 arithmetic -- element-wise .rn operations
+// on independent lanes, so each value's rounding sequence is dot_avx's:
+//   a..d (pairs of lanes) = fma(w, x, 0); lanes = (a + b) + (c + d);
+//   (h0, h1) = lanes[0:2] + lanes[4:6], (h2, h3) = lanes[2:4] + lanes[6:8];
+//   partial = (h0 + h2) + (h1 + h3).
+// The walker warp then runs each row's ordered chain
+// result = fma(partial_g, scale_g, result) over the groups of stage s while
+// the compute warps work on stage s + 1 (partials double-buffered; named
+// barriers: kReady + b when buffer b is written, kFree + b when it is read).
+constexpr int kCompute32 = 512;
+constexpr int kThreads32 = kCompute32 + 64;
+constexpr int kBarReady = 1, kBarFree = 3;
+
+__device__ __forceinline__ unsigned long long pack2(float lo, float hi) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ float2 unpack2(unsigned long long v) {
+    float2 r;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+    return r;
+}
+__device__ __forceinline__ unsigned long long add2(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ unsigned long long sub2(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ unsigned long long fma2(unsigned long long a, unsigned long long b,
+                                                   unsigned long long c) {
+    unsigned long long d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ void bar_arrive(int id, int count) {
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+__device__ __forceinline__ void bar_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+__global__ void __launch_bounds__(kThreads32, 1) gemv_w4a32_g32_kernel(const W4Args a) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const int S = a.stages;
+    const int G = a.groups;
+    const int row_bytes = static_cast<int>(a.cols / 2);
+    const int w_bytes = kRowsPerStage * row_bytes;
+    const int s_bytes = kRowsPerStage * G * 4;
+    const int stage_bytes = w_bytes + s_bytes;
+    const int pstride = G + 1;
+    uint8_t* stages = smem;
+    float* P = reinterpret_cast<float*>(smem + (size_t)S * stage_bytes);  // [2][RS][G+1]
+    float* SC = P + 2 * kRowsPerStage * pstride;                          // [2][RS][G+1]
+    uint64_t* full = reinterpret_cast<uint64_t*>(SC + 2 * kRowsPerStage * pstride);
+    uint64_t* empty = full + S;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + S);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t row0 = (int64_t)blockIdx.x * a.rows / gridDim.x;
+    const int64_t row1 = (int64_t)(blockIdx.x + 1) * a.rows / gridDim.x;
+    const int nblocks = static_cast<int>((row1 - row0 + kRowsPerStage - 1) / kRowsPerStage);
+    constexpr int kWalker = kCompute32 / 32, kProducer = kWalker + 1;
+    constexpr int kParties = kCompute32 + 32;  // compute warps + walker
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kCompute32 / 32);
+        }
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+    grid_launch_dependents();
+
+    if (warp == kProducer) {
+        if (lane == 0) {
+            const uint64_t policy = l2_policy_evict_first();
+            for (int s = 0; s < nblocks; ++s) {
+                const int buf = s % S;
+                if (s >= S && !mbar_wait(&empty[buf], ((s / S) - 1) & 1, kSiteW4Empty)) break;
+                const int64_t r = row0 + (int64_t)s * kRowsPerStage;
+                const int live = static_cast<int>(min64(kRowsPerStage, row1 - r));
+                uint8_t* dst = stages + (size_t)buf * stage_bytes;
+                mbar_arrive_expect_tx(&full[buf], static_cast<uint32_t>(live * (row_bytes + G * 4)));
+                bulk_copy_g2s(dst, a.w + r * row_bytes, static_cast<uint32_t>(live * row_bytes), &full[buf],
+                              policy);
+                bulk_copy_g2s(dst + w_bytes, a.ws + r * G, static_cast<uint32_t>(live * G * 4), &full[buf],
+                              policy);
+            }
+        }
+        return;
+    }
+
+    if (warp == kWalker) {
+        // Each row's groups in order: result = fma(partial, scale, result).
+        float bias_r = 0.0f;
+        for (int s = 0; s < nblocks; ++s) {
+            const int pb = s & 1;
+            const int64_t r0 = row0 + (int64_t)s * kRowsPerStage;
+            const int live = static_cast<int>(min64(kRowsPerStage, row1 - r0));
+            if (lane < live) bias_r = a.bias ? __ldg(a.bias + r0 + lane) : 0.0f;
+            bar_sync(kBarReady + pb, kParties);
+            if (!*abort_flag && lane < live) {
+                const float* pr = P + (pb * kRowsPerStage + lane) * pstride;
+                const float* sr = SC + (pb * kRowsPerStage + lane) * pstride;
+                // Loads run 16 groups ahead of the dependent FMAs.
+                float result = 0.0f;
+#pragma unroll 16
+    #pragma unroll 16
+            for (int k = 0; k < G; ++k) result = __fmaf_rn(pr[k], sr[k], result);
+                a.y[r0 + lane] = __fadd_rn(result, bias_r);
+            }
+            bar_arrive(kBarFree + pb, kParties);
+        }
+        return;
+    }
+
+    // ---------------------------------------------------------- compute warps
+    grid_dependency_wait();
+    const int tid = threadIdx.x;
+    const int slots = kCompute32 / G;  // >= 1
+    const int g = tid % G;
+    const int slot = tid / G;
+    const bool active = slot < slots;
+    unsigned long long x2[16];  // x[32 g + 2i], x[32 g + 2i + 1]
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 v = active ? __ldg(reinterpret_cast<const float4*>(a.x + (int64_t)g * 32) + i)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+        x2[2 * i] = pack2(v.x, v.y);
+        x2[2 * i + 1] = pack2(v.z, v.w);
+    }
+    const unsigned long long bias2 = pack2(8388616.0f, 8388616.0f);  // 2^23 + 8
+    const unsigned long long zero2 = pack2(0.0f, 0.0f);
+    for (int s = 0; s < nblocks; ++s) {
+        const int buf = s % S;
+        const int pb = s & 1;
+        const int64_t r0 = row0 + (int64_t)s * kRowsPerStage;
+        const int live = static_cast<int>(min64(kRowsPerStage, row1 - r0));
+        const bool landed = mbar_wait(&full[buf], (s / S) & 1, kSiteW4Full);
+        if (!landed) *abort_flag = 1;
+        if (s >= 2) bar_sync(kBarFree + pb, kParties);  // the walker is done with buffer pb
+        const uint8_t* sw = stages + (size_t)buf * stage_bytes;
+        const float* sscale = reinterpret_cast<const float*>(sw + w_bytes);
+        if (landed && active) {
+            for (int r = slot; r < live; r += slots) {
+                const uint4 v = *reinterpret_cast<const uint4*>(sw + (size_t)r * row_bytes + (size_t)g * 16);
+                const uint32_t words[4] = {v.x, v.y, v.z, v.w};
+                unsigned long long L[4];  // (lanes[2i], lanes[2i+1])
+                unsigned long long acc[4][4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    // word j = columns 8j..8j+7: column 8j+2i is the low nibble of
+                    // byte i, column 8j+2i+1 its high nibble.
+                    const uint32_t even = (words[j] & 0x0f0f0f0fu) ^ 0x08080808u;
+                    const uint32_t odd = ((words[j] >> 4) & 0x0f0f0f0fu) ^ 0x08080808u;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const uint32_t lo = __byte_perm(even, 0x4B000000u, 0x7540u | i);
+                        const uint32_t hi = __byte_perm(odd, 0x4B000000u, 0x7540u | i);
+                        const unsigned long long w = sub2(pack2(__uint_as_float(lo), __uint_as_float(hi)), bias2);
+                        acc[j][i] = fma2(w, x2[4 * j + i], zero2);
+                    }
+                }
+#pragma unroll
+                for (int i = 0; i < 4; ++i) L[i] = add2(add2(acc[0][i], acc[1][i]), add2(acc[2][i], acc[3][i]));
+                const unsigned long long h01 = add2(L[0], L[2]);  // (h0, h1)
+                const unsigned long long h23 = add2(L[1], L[3]);  // (h2, h3)
+                const unsigned long long q = add2(h01, h23);      // (h0 + h2, h1 + h3)
+                const float2 qq = unpack2(q);
+                P[(pb * kRowsPerStage + r) * pstride + g] = __fadd_rn(qq.x, qq.y);
+                SC[(pb * kRowsPerStage + r) * pstride + g] = sscale[r * G + g];
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[buf]);
+        bar_arrive(kBarReady + pb, kParties);
     }
 }
 
@@ -197,7 +393,7 @@ bool gemv_w4a32_fast_supported(int64_t tokens, int64_t cols, int bits, int64_t g
     if (group != 32 && group != 64 && group != 128) return false;
     if (cols % group != 0 || cols % 32 != 0) return false;
     const int64_t groups = cols / group;
-    if (groups > kConsumers || groups % 4 != 0) return false;
+    if (groups > kConsumers || groups % 4 != 0) return false;  // also covers the 32-column kernel (512 threads)
     return aligned16(weight) && aligned16(wscales);
 }
 
@@ -226,6 +422,21 @@ int launch_gemv_w4a32_fast(cudaStream_t s, const float* x, int64_t cols, const u
                         static_cast<int64_t>(stage_bytes + 16);
     if (fit < 1) return LEAFQ_ERR_UNSUPPORTED;
     a.stages = static_cast<int>(std::min<int64_t>(fit, max_stages));
+    if (group == 32) {
+        // Two partial buffers for the walker.
+        const size_t fixed32 = 2 * fixed;
+        const int64_t fit32 = (static_cast<int64_t>(budget) - static_cast<int64_t>(fixed32)) /
+                              static_cast<int64_t>(stage_bytes + 16);
+        if (fit32 >= 2) {
+            W4Args b = a;
+            b.stages = static_cast<int>(std::min<int64_t>(fit32, max_stages));
+            const size_t smem32 = stage_bytes * b.stages + fixed32 + 16 * b.stages + 16;
+            const void* fn = reinterpret_cast<const void*>(gemv_w4a32_g32_kernel);
+            int st = allow_smem(fn, smem32, "gemv_w4a32_g32");
+            if (st) return st;
+            return launch(gemv_w4a32_g32_kernel, dim3(grid), dim3(kThreads32), smem32, s, pdl, "gemv_w4a32_g32", b);
+        }
+    }
     const size_t smem = stage_bytes * a.stages + fixed + 16 * a.stages + 16;  // + abort flag
     switch (group) {
         case 32: return launch_gs<32>(s, a, grid, smem, pdl);

@@ -4,7 +4,9 @@
 // quantisation, :1221-1231 with quant_dot_avx :536-570) for per-row INT8
 // weights (group == cols, the default export) and 1..8 tokens.
 //
-// Layout of one block (two per SM, up to 100 KB of shared memory each):
+// Layout of one block (two per SM for a call, up to 100 KB of shared memory
+// each; small slices are sized by their rows so that the next call's blocks
+// fit beside them):
 //   warp 8 (producer): streams this block's contiguous slice of weight rows
 //     into a ring of stages with 1-D bulk copies (cp.async.bulk, TMA engine,
 //     evict-first L2 policy).  A stage holds one chunk (<= 2 KB) of 16 rows.
@@ -21,8 +23,9 @@
 //       y = fma(float(acc) * sx, sw, 0.0f) + (bias or 0.0f)
 //     which is the reference's result[t] += float(acc) * sx * sw (fused by
 //     GCC into one FMA, decoder.cpp:567) followed by + bias (:1229).
-//   Two blocks per SM (half the shared memory each), so twice the warps
-//   hide the per-row latency of the dot, reduction and epilogue.
+//   Two blocks per SM (grid 2 x SMs), so twice the warps hide the per-row
+//   latency of the dot, reduction and epilogue; registers are capped so that
+//   four blocks fit, two of this call and two of the next.
 // Bytes per call: rows * cols (weights) + 4 * rows (scales) [+ 4 * rows bias]
 //   + 4 * tokens * (cols + rows): HBM-bound.
 #include "leafq_device.cuh"
@@ -55,6 +58,7 @@ struct GemvArgs {
     int nchunks;  // ceil(cols / chunk)
     int stages;   // ring depth
     int qstride;  // bytes between token rows of the code buffer
+    int stage_area;  // bytes of shared memory holding the stages (the codes follow)
     PeerStore peer;  // fused all-gather epilogue when peer.world > 0
 };
 
@@ -68,13 +72,16 @@ __device__ __forceinline__ int8_t to_code(float v, float multiplier) {
     return static_cast<int8_t>(r);
 }
 
+// Four blocks per SM (56 registers): under programmatic dependent launch the
+// next GEMV's two blocks per SM become resident beside this one's and
+// stream their weights while this one computes.
 template <int MAXT>
-__global__ void __launch_bounds__(kThreads, 2) gemv_w8a8_kernel(const GemvArgs a) {
+__global__ void __launch_bounds__(kThreads, 4) gemv_w8a8_kernel(const GemvArgs a) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const int S = a.stages;
     const int chunk = a.chunk;
     uint8_t* stage_base = smem;
-    int8_t* codes = reinterpret_cast<int8_t*>(smem + (size_t)S * kRowsPerStage * chunk);
+    int8_t* codes = reinterpret_cast<int8_t*>(smem + a.stage_area);
     float* token_scale = reinterpret_cast<float*>(codes + MAXT * a.qstride);
     uint64_t* full = reinterpret_cast<uint64_t*>(token_scale + 8);
     uint64_t* empty = full + S;
@@ -140,9 +147,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_w8a8_kernel(const GemvArgs a
     // The run tag of a fused all-gather (written by the previous collect).
     const uint32_t tag = a.peer.world ? *reinterpret_cast<const volatile uint32_t*>(a.peer.epoch) : 0u;
     // Per-token absmax (exact, order-free), scale and multiplier.  With one
-    // or two tokens and cols <= 8192, x stays in registers between the
+    // or two tokens and cols <= 2048, x stays in registers between the
     // absmax pass and the coding pass (one read of x instead of two).
-    constexpr int kXRegs = MAXT <= 2 ? 8 : 1;
+    constexpr int kXRegs = MAXT <= 2 ? 2 : 1;
     const int64_t vecs = a.cols / 4;
     const bool x_in_regs = MAXT <= 2 && vecs <= (int64_t)kXRegs * nthreads;
     float4 xr[MAXT][kXRegs];
@@ -336,7 +343,16 @@ int launch_gemv_w8a8(cudaStream_t s, const float* x, int64_t tokens, int64_t col
                   static_cast<int64_t>(stage_bytes + 16);
     if (fit < 1) return LEAFQ_ERR_UNSUPPORTED;
     a.stages = static_cast<int>(std::min<int64_t>(fit, max_stages));
-    const size_t smem = stage_bytes * a.stages + fixed + 16 * a.stages;
+    // When the whole row slice is resident (every stage its own buffer) and
+    // rows are one chunk wide, the last buffer only holds the slice's last
+    // rows: size the shared memory by the rows, so that four blocks fit on
+    // an SM (a config-0 slice of 20 rows x 2 KB: 42 KB instead of 66 KB).
+    a.stage_area = static_cast<int>(stage_bytes * a.stages);
+    if (a.stages == max_stages && a.nchunks == 1) {
+        const int64_t last_rows = max_rows - (int64_t)kRowsPerStage * (a.stages - 1);
+        a.stage_area = static_cast<int>(stage_bytes * (a.stages - 1) + (size_t)last_rows * a.chunk);
+    }
+    const size_t smem = (size_t)a.stage_area + fixed + 16 * a.stages;
     switch (maxt) {
         case 1: return launch_t<1>(s, a, grid, smem, pdl);
         case 2: return launch_t<2>(s, a, grid, smem, pdl);

@@ -287,16 +287,27 @@ graph_gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_con
                 tmem_wait_ld();
                 const int64_t nb = n0 + c;
                 if (!live || nb >= g.n) continue;
-#pragma unroll 8
+                float v[32];
+#pragma unroll
                 for (int j = 0; j < 32; ++j) {
-                    if (nb + j >= g.n) break;
                     // (float(acc) * input_scale) * weight_scales[col] (+ bias), gemm.cpp:150-160.
                     float value = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[j])), g.input_scale),
                                             ws_s[c + j]);
                     if (g.bias) value = __fadd_rn(value, bias_s[c + j]);
                     if (g.relu) value = value < 0.0f ? 0.0f : value;
-                    if (g.glue.on) value = graph_glue(value, g.glue, row, nb + j, g.n, *tab);
-                    out[nb + j] = value;
+                    if (g.glue.on && nb + j < g.n) value = graph_glue(value, g.glue, row, nb + j, g.n, *tab);
+                    v[j] = value;
+                }
+                // 32 consecutive outputs of this row: float4 stores when the row
+                // segment is whole and 16-byte aligned.
+                if (nb + 32 <= g.n && ((reinterpret_cast<uintptr_t>(out + nb) & 15u) == 0)) {
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4)
+                        *reinterpret_cast<float4*>(out + nb + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (nb + j < g.n) out[nb + j] = v[j];
                 }
             }
             tcgen05_fence_before();
