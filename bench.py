@@ -89,6 +89,7 @@ CASES = {
     "gemm_down": (512, 2048, 5632, 8, 5632, 8),  # config 2 down_proj shape
     "gemm_big": (4096, 5632, 2048, 8, 2048, 8),  # large-M prefill
     "w4": (1, 11008, 4096, 4, 32, 32),          # config 1 INT4 weight-only GEMV
+    "graph_gemm": None,                          # graph INT8 GEMM, [k, n] weight, m=512 k=2048 n=5632
     "decode_small": None,                        # persistent decode kernel, 3-layer stack
     "model_small": None,                         # whole-model decode kernel, 3-layer model
     "batch_step": None,                          # config 4: 64 x 512 prefill + 2 decode steps, 22 layers
@@ -142,6 +143,24 @@ def run_case(name):
         if dec.device_status() != 0:
             raise RuntimeError("device status not ok")
         print(json.dumps({"case": name, "layers": layers, "sequences": BATCH_SEQUENCES, "status": "ok"}))
+        return
+    if name == "graph_gemm":
+        # The graph executor's gemm_i8_per_channel on the tensor cores, its
+        # weight [k, n] as the graph stores it (read MN-major).
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(0)
+        m, k, n = 512, 2048, 5632
+        a = torch.randint(-127, 128, (m, k), generator=gen, device=dev, dtype=torch.int8)
+        b = torch.randint(-127, 128, (k, n), generator=gen, device=dev, dtype=torch.int8)
+        sc = torch.rand(n, generator=gen, device=dev) * 0.01
+        for _ in range(3):
+            lq.gemm_i8_per_channel(a, b, None, 0.01, sc)
+        torch.cuda.synchronize()
+        if lq.load().leafq_device_status() != 0:
+            raise RuntimeError("device status not ok")
+        print(json.dumps({"case": name, "m": m, "k": k, "n": n, "status": "ok"}))
         return
     if name == "decode_small":
         # The persistent decode kernel on a 3-layer TinyLlama-width stack
