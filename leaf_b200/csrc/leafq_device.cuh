@@ -167,6 +167,41 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
         : "memory");
 }
 
+// 2-D tiled tensor store shared -> global (bulk group).  c0 is the inner
+// coordinate in elements (its byte offset a multiple of 16), c1 the row;
+// both non-negative.  Elements outside the tensor are not written.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* smem_src, int32_t c0, int32_t c1) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(map), "r"(c0),
+                 "r"(c1), "r"(smem_u32(smem_src))
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until this thread's committed bulk stores have finished reading
+// shared memory (the source may be rewritten) / have completed.
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// One 32 x 32 fp32 block of an output tile: lane r of the warp holds row r's
+// 32 values (v), written into a 4 KB shared-memory tile in the 128-byte
+// swizzled layout a TMA store reads (16-byte chunk i of row r at chunk
+// i ^ (r % 8): the lanes of each float4 store hit all 32 banks), then
+// stored by one TMA from lane 0.  The tile's previous store must have
+// finished reading (the caller waits before writing again).
+__device__ __forceinline__ void store_block_32x32(float* tile, const float (&v)[32], int lane,
+                                                  const CUtensorMap* map, int32_t c0, int32_t c1, bool issue) {
+    uint8_t* row = reinterpret_cast<uint8_t*>(tile) + lane * 128;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+        *reinterpret_cast<float4*>(row + ((i ^ (lane & 7)) << 4)) =
+            make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0 && issue) {
+        tma_store_2d(map, tile, c0, c1);
+        bulk_commit_group();
+    }
+}
+
 // Prefetch `bytes` (multiple of 16, 16-byte aligned) of global memory into L2.
 __device__ __forceinline__ void bulk_prefetch_l2(const void* gmem_src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gmem_src), "r"(bytes) : "memory");
@@ -300,11 +335,89 @@ __host__ __device__ constexpr uint32_t umma_idesc_i8(uint32_t m, uint32_t n) {
     return (2u << 4) | (1u << 7) | (1u << 10) | ((n >> 3) << 17) | ((m >> 4) << 24);
 }
 
+// ------------------------------------------------ CTA pairs (2-SM MMA)
+// A cluster of two CTAs on two SMs: the leader (rank 0) issues
+// tcgen05.mma.cta_group::2 over both CTAs' shared-memory halves.  No copy
+// here uses multicast; only tcgen05.commit multicasts its arrival.
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// Shared::cluster address of `local` (a shared::cta address) in CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t local, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+    return r;
+}
+
+// All threads of both CTAs.
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// 2-D tiled load into this CTA's shared memory whose completion is counted
+// on an mbarrier of either CTA of the pair (`mbar` a shared::cluster
+// address).  No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, int32_t c0, int32_t c1,
+                                                 uint32_t mbar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        ".L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(smem_dst)),
+        "l"(map), "r"(c0), "r"(c1), "r"(mbar), "l"(policy)
+        : "memory");
+}
+
+// Arrive on an mbarrier of either CTA (shared::cluster address).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t mbar) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(mbar) : "memory");
+}
+
+// TMEM allocation for a CTA pair: one warp of each CTA, the same warp index
+// and the same destination offset in both.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_result, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_result)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// D[tmem of both CTAs] (+)= A[each CTA's half of M] * B[both CTAs' halves of N]^T.
+__device__ __forceinline__ void umma_i8_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrive once on the mbarrier at `bar`'s offset in every CTA of `cta_mask`
+// when the pair's previously issued MMAs have completed.
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar, uint16_t cta_mask) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_u32(bar)),
+        "h"(cta_mask)
+        : "memory");
+}
+
 // 2-D tensor map over a row-major uint8 [outer, inner] matrix (inner
 // contiguous, a multiple of 16 bytes) with 128-byte swizzle and box
 // [box_outer, box_inner]; out-of-range elements load as zero.  Host side.
 int make_tma_map_u8(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, int box_inner,
                     int box_outer);
+// The same for a row-major fp32 [outer, inner] matrix (inner a multiple of
+// 4), box [32 rows, 32 floats], 128-byte swizzle: the output blocks of
+// store_block_32x32.
+int make_tma_map_f32_out(CUtensorMap* map, const void* base, int64_t inner, int64_t outer);
 
 // Instruction descriptor for kind::i8 with the B operand MN-major (bit 16):
 // B tiles hold rows of N contiguous, as a [k, n] matrix is stored.
