@@ -797,6 +797,20 @@ def linear_rates(device, peak_gbs):
                                           "method": "8 distinct weights back to back in one CUDA graph "
                                                     "(activation quantisation included)"}
         del wl, yl
+    # The same prefill GEMM at 4096 tokens (CTA-pair tiles), quantisation included.
+    big = 4096
+    xb = torch.randn(big, 2048, generator=gen, device=device)
+    wl = [random_w8_weight(5632, 2048, gen, device) for _ in range(4)]
+    yl = [torch.empty(big, 5632, device=device) for _ in wl]
+    us = timed([lambda w=w, y=y: lq.linear(xb, w, out=y, workspace=ws, flags=LEAFQ_FLAG_PDL) for w, y in zip(wl, yl)],
+               reps=5)
+    tops = 2.0 * big * 5632 * 2048 / (us * 1e-6) / 1e12
+    out["gemm_m4096_n5632_k2048"] = {"us_per_call": us, "achieved": tops, "unit": "TOP/s", "peak": peak_top,
+                                     "frac": tops / peak_top,
+                                     "peak_source": "2 x measured bf16 burst (no INT8 figure measured)",
+                                     "method": "4 distinct weights back to back in one CUDA graph "
+                                               "(activation quantisation included)"}
+    del wl, yl, xb
     # The graph executor's INT8 GEMM (gemm_i8_per_channel) at the config-2
     # shape with its weight as the graph stores it, [k, n] (read MN-major by
     # the tensor cores): 8 distinct weights, codes given.
