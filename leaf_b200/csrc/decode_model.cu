@@ -377,8 +377,13 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
             // ---------------------------------------------- attention
             // Cached keys / values of rows [0, pos) are staged through the
             // attention region (the ring's last 64 KB, the codes buffer and
-            // the scratch: free in this block now) in chunks of C rows; chunk
-            // 0 of both is requested before the wait for this token's q, k, v.
+            // the scratch: free in this block now).  When all keys and values
+            // fit side by side, both are requested before the wait for this
+            // token's q, k, v.  Otherwise the whole region holds keys for the
+            // scores (one chunk up to ~320 keys of 64 floats), and then values
+            // for the weighted sums, requested as soon as the scores are done
+            // so that they land during the softmax (instead of a second key
+            // and a second value chunk each waited for after the first).
             // Values come in one bulk copy per chunk.  Keys come as 16-byte
             // asynchronous copies by all consumer threads into rows padded by
             // 4 floats, so the 8 lanes of a quarter warp, each reading a float4
@@ -395,20 +400,25 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
             const int keys_r = static_cast<int>((keys + 3) & ~3);
             float* scores = att;
             const int kst = dim + 4;  // padded key row (floats)
-            const int chunk = static_cast<int>(min64((kAttFloats - keys_r) / (kst + dim), pos > 0 ? pos : 1));
+            const int avail = kAttFloats - keys_r;
+            const int64_t least = pos > 0 ? pos : 1;
+            const bool side_by_side = avail / (kst + dim) >= least;
+            const int kchunk = static_cast<int>(side_by_side ? least : min64(avail / kst, least));
+            const int vchunk = static_cast<int>(side_by_side ? least : min64(avail / dim, least));
             float* kbuf = att + keys_r;
-            float* vbuf = kbuf + chunk * kst;
+            float* vbuf = side_by_side ? kbuf + kchunk * kst : kbuf;
             const uint64_t keep = l2_policy_evict_last();
-            const int nchunks = static_cast<int>((pos + chunk - 1) / chunk);
+            const int nchunks = static_cast<int>((pos + kchunk - 1) / kchunk);    // key chunks
+            const int nvchunks = static_cast<int>((pos + vchunk - 1) / vchunk);  // value chunks
             auto issue = [&](const float* base, float* dst, uint64_t* bar, int c) {
-                const int64_t k0 = (int64_t)c * chunk;
-                const uint32_t bytes = static_cast<uint32_t>(min64(chunk, pos - k0) * dim * sizeof(float));
+                const int64_t k0 = (int64_t)c * vchunk;
+                const uint32_t bytes = static_cast<uint32_t>(min64(vchunk, pos - k0) * dim * sizeof(float));
                 mbar_arrive_expect_tx(bar, bytes);
                 bulk_copy_g2s(dst, base + k0 * dim, bytes, bar, keep);
             };
             auto load_keys = [&](int c) {  // every consumer thread; completed by wait_async_copies()
-                const int64_t k0 = (int64_t)c * chunk;
-                const int rows = static_cast<int>(min64(chunk, pos - k0));
+                const int64_t k0 = (int64_t)c * kchunk;
+                const int rows = static_cast<int>(min64(kchunk, pos - k0));
                 const int vpr = dim / 4;
                 for (int i = tid; i < rows * vpr; i += kNC) {
                     const int r = i / vpr, q = i - r * vpr;
@@ -418,7 +428,7 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
             };
             consumer_sync();  // every warp is done with the previous linear's codes
             if (nchunks > 0) load_keys(0);
-            if (tid == 0 && nchunks > 0) issue(vc, vbuf, &att_bar[1], 0);
+            if (tid == 0 && nvchunks > 0 && side_by_side) issue(vc, vbuf, &att_bar[1], 0);
             // This position's rotation (independent of q and k), before the wait.
             float rope_c = 0.0f, rope_s = 0.0f;
             if (tid < half) {
@@ -464,8 +474,8 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
                 local_max = sc;
             }
             for (int c = 0; c < nchunks; ++c) {
-                const int64_t k0 = (int64_t)c * chunk;
-                const int nk = static_cast<int>(min64(chunk, pos - k0));
+                const int64_t k0 = (int64_t)c * kchunk;
+                const int nk = static_cast<int>(min64(kchunk, pos - k0));
                 if (c > 0) load_keys(c);
                 wait_async_copies();
                 consumer_sync();
@@ -486,6 +496,9 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
                 }
                 consumer_sync();  // chunk consumed
             }
+            // The keys are consumed: values into the same region now, while
+            // the softmax runs.
+            if (tid == 0 && nvchunks > 0 && !side_by_side) issue(vc, vbuf, &att_bar[1], 0);
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) local_max = fmaxf(local_max, __shfl_xor_sync(0xffffffffu, local_max, o));
             if (lane == 0) partial_max[warp] = local_max;
@@ -514,9 +527,9 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
             consumer_sync();
             // out[d] = sum over keys, in order, of probability * v[k][d].
             float acc = 0.0f;
-            for (int c = 0; c < nchunks; ++c) {
-                const int64_t k0 = (int64_t)c * chunk;
-                const int nk = static_cast<int>(min64(chunk, pos - k0));
+            for (int c = 0; c < nvchunks; ++c) {
+                const int64_t k0 = (int64_t)c * vchunk;
+                const int nk = static_cast<int>(min64(vchunk, pos - k0));
                 if (c > 0 && tid == 0) issue(vc, vbuf, &att_bar[1], c);
                 if (ok && !mbar_wait(&att_bar[1], att_uses[1] & 1, kSiteDecodeFull)) {
                     ok = false;
