@@ -17,7 +17,12 @@ device (no host round trip per token).
 
 Supported artifacts: RMSNorm, RoPE, gated SiLU, sequential residual, no
 sliding window, no Q/K norm (the Llama / Mistral-without-window / Qwen2
-family); anything else raises.
+family); anything else raises.  Linear biases (q / k / v in Qwen2 exports) are
+added in the linears' epilogues; SmoothQuant input scales
+(``<proj>.input_scale``, decoder.cpp:1008-1019) are applied inside each
+projection's quantiser, which runs q / k / v and gate / up as separate
+linears (their inputs are scaled differently).  Such artifacts take the
+per-operator path; the one-launch step needs the plain per-row INT8 export.
 """
 from __future__ import annotations
 
@@ -44,9 +49,14 @@ def _on(a, device: torch.device) -> torch.Tensor:
     return torch.from_numpy(np.array(a)).to(device)
 
 
-def _concat_rows(parts: list[HostTensor], device: torch.device, interleave: bool = False) -> QuantWeight:
+def _concat_rows(parts: list[HostTensor], device: torch.device, interleave: bool = False,
+                 biases=None, input_scale=None) -> QuantWeight:
     """Rows of several equally quantised matrices as one weight: stacked
-    (q | k | v) or, with interleave, alternating (gate_0, up_0, gate_1, ...)."""
+    (q | k | v) or, with interleave, alternating (gate_0, up_0, gate_1, ...).
+    biases: one HostTensor or None per part (a missing bias adds 0.0f, as the
+    reference's output = result + 0 would not: only parts with a bias get
+    one, so a stack mixing both is rejected); input_scale: the calibrated
+    SmoothQuant factors of a single part."""
     bits, group, cols = parts[0].bits, parts[0].group, parts[0].cols
     if any(p.bits != bits or p.group != group or p.cols != cols for p in parts):
         raise LeafError(_lib.LEAFQ_ERR_UNSUPPORTED, "fused projections need one precision and group")
@@ -59,8 +69,15 @@ def _concat_rows(parts: list[HostTensor], device: torch.device, interleave: bool
         data = torch.cat(datas, dim=0)
         scales = None if scales is None else torch.cat(scales, dim=0)
     rows = sum(p.rows for p in parts)
+    bias = None
+    if biases is not None and any(b is not None for b in biases):
+        if any(b is None for b in biases):
+            raise LeafError(_lib.LEAFQ_ERR_UNSUPPORTED, "stacked projections with and without biases")
+        vecs = [_on(b.data, device).to(torch.float32).reshape(-1) for b in biases]
+        bias = (torch.stack(vecs, dim=1).reshape(-1) if interleave else torch.cat(vecs)).contiguous()
+    scale = None if input_scale is None else _on(input_scale.data, device).to(torch.float32).reshape(-1).contiguous()
     w = QuantWeight(data.contiguous(), None if scales is None else scales.contiguous(), rows, cols, bits,
-                    group if bits != 32 else 0)
+                    group if bits != 32 else 0, bias, scale)
     w.check()
     return w
 
@@ -125,41 +142,47 @@ class Decoder:
         def f32(t: HostTensor):
             return _on(t.data, dev).to(torch.float32).reshape(-1).contiguous()
 
-        def weight(parts, interleave=False):
-            return self._shard(_concat_rows(parts, dev, interleave))
+        def weight(parts, interleave=False, biases=None, input_scale=None):
+            return self._shard(_concat_rows(parts, dev, interleave, biases, input_scale))
 
         emb = art.get("model.embed_tokens.weight")
         self.embed_table = _on(emb.data, dev).contiguous()
         self.embed_scales = None if emb.scales is None else _on(emb.scales, dev).contiguous()
         self.embed_bits, self.embed_group = emb.bits, emb.group
+        # SmoothQuant artifacts (decoder.cpp:1008-1019) carry per-projection
+        # input scales: q, k, v (and gate, up) then cannot share one
+        # quantisation of their common input and run as separate linears.
+        self.smooth = any(art.get(f"model.layers.{i}.{n}.input_scale") is not None for i in range(cfg.layers)
+                          for n in ("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj", "self_attn.o_proj",
+                                    "mlp.gate_proj", "mlp.up_proj", "mlp.down_proj"))
+        self.has_bias = False
         self.layers = []
         for i in range(cfg.layers):
             p = f"model.layers.{i}."
             get = art.get
-            self.layers.append(dict(
-                input_norm=f32(get(p + "input_layernorm.weight")),
-                post_norm=f32(get(p + "post_attention_layernorm.weight")),
-                qkv=weight([get(p + "self_attn.q_proj.weight"), get(p + "self_attn.k_proj.weight"),
-                            get(p + "self_attn.v_proj.weight")]),
-                o=weight([get(p + "self_attn.o_proj.weight")]),
-                gate_up=weight([get(p + "mlp.gate_proj.weight"), get(p + "mlp.up_proj.weight")],
-                               interleave=True),
-                down=weight([get(p + "mlp.down_proj.weight")]),
-            ))
-            for name in ("q", "k", "v", "o"):
-                if get(p + f"self_attn.{name}_proj.bias") is not None:
-                    raise LeafError(_lib.LEAFQ_ERR_UNSUPPORTED, "projection biases are not supported")
-            smoothed = [p + f"self_attn.{n}_proj.input_scale" for n in ("q", "k", "v", "o")] + \
-                       [p + f"mlp.{n}_proj.input_scale" for n in ("gate", "up", "down")]
-            if any(get(n) is not None for n in smoothed):
-                # SmoothQuant factors differ per projection, so q|k|v and
-                # gate|up cannot share one quantisation; their linears run
-                # one by one through leafq_linear_smooth instead.
-                raise LeafError(_lib.LEAFQ_ERR_UNSUPPORTED,
-                                "the GPU decoder does not take SmoothQuant artifacts (input_scale tensors); "
-                                "run their linears with leafq_linear_smooth")
+            names = {n: p + m for n, m in (("q", "self_attn.q_proj"), ("k", "self_attn.k_proj"),
+                                           ("v", "self_attn.v_proj"), ("o", "self_attn.o_proj"),
+                                           ("gate", "mlp.gate_proj"), ("up", "mlp.up_proj"),
+                                           ("down", "mlp.down_proj"))}
+            wt = {n: get(b + ".weight") for n, b in names.items()}
+            bias = {n: get(b + ".bias") for n, b in names.items()}
+            scale = {n: get(b + ".input_scale") for n, b in names.items()}
+            self.has_bias |= any(b is not None for b in bias.values())
+            layer = dict(input_norm=f32(get(p + "input_layernorm.weight")),
+                         post_norm=f32(get(p + "post_attention_layernorm.weight")),
+                         o=weight([wt["o"]], biases=[bias["o"]], input_scale=scale["o"]),
+                         down=weight([wt["down"]], biases=[bias["down"]], input_scale=scale["down"]))
+            if self.smooth:
+                for n in ("q", "k", "v", "gate", "up"):
+                    layer[n] = weight([wt[n]], biases=[bias[n]], input_scale=scale[n])
+            else:
+                layer["qkv"] = weight([wt["q"], wt["k"], wt["v"]], biases=[bias["q"], bias["k"], bias["v"]])
+                layer["gate_up"] = weight([wt["gate"], wt["up"]], interleave=True,
+                                          biases=[bias["gate"], bias["up"]])
+            self.layers.append(layer)
         self.final_norm = f32(art.get("model.norm.weight")) if cfg.final_norm else None
-        self.lm_head = weight([art.get("lm_head.weight")])
+        self.lm_head = weight([art.get("lm_head.weight")], biases=[art.get("lm_head.bias")])
+        self.has_bias |= self.lm_head.bias is not None
         d, kv = cfg.head_dim, cfg.kv_heads
         S = self.sequences
         self.k_cache = [torch.zeros((S, kv, self.capacity, d), dtype=torch.float32, device=dev)
@@ -203,6 +226,8 @@ class Decoder:
                      gate_up=e(rows, 2 * c.intermediate), act=e(rows, c.intermediate),
                      down=e(rows, c.hidden), last=e(S, c.hidden), logits=e(S, c.vocab),
                      workspace=Workspace(dev),
+                     q=e(rows, q), k=e(rows, c.kv_heads * c.head_dim), v=e(rows, c.kv_heads * c.head_dim),
+                     gate=e(rows, c.intermediate), up=e(rows, c.intermediate),
                      codes=torch.empty((rows, c.hidden), dtype=torch.int8, device=dev),
                      codes_mlp=torch.empty((rows, c.intermediate), dtype=torch.int8, device=dev),
                      code_scales=e(rows))
@@ -210,8 +235,7 @@ class Decoder:
             # keeps its pointers, so nothing it uses may be reallocated.
             for w in self._weights():
                 for r in (rows, S):
-                    need = self.lib.leafq_linear_workspace_bytes(r, w.cols, w.bits, w.group,
-                                                                 self.activation_bits)
+                    need = self._workspace_bytes(w, r)
                     if need:
                         b["workspace"].get(need)
             need = self.lib.leafq_attention_workspace_bytes(S, tokens, c.heads, c.kv_heads, c.head_dim,
@@ -222,7 +246,9 @@ class Decoder:
 
     def _weights(self):
         for layer in self.layers:
-            yield from (layer["qkv"], layer["o"], layer["gate_up"], layer["down"])
+            for n in ("qkv", "q", "k", "v", "o", "gate_up", "gate", "up", "down"):
+                if n in layer:
+                    yield layer[n]
         yield self.lm_head
 
     # ------------------------------------------------------- row sharding
@@ -238,7 +264,8 @@ class Decoder:
                             f"{w.rows} rows do not split evenly over {self.world} ranks")
         b, e = part.begin(self.rank), part.end(self.rank)
         shard = QuantWeight(w.data[b:e].clone(), None if w.scales is None else w.scales[b:e].clone(), e - b,
-                            w.cols, w.bits, w.group)
+                            w.cols, w.bits, w.group, None if w.bias is None else w.bias[b:e].clone(),
+                            w.input_scale)
         self._full_rows[id(shard)] = w.rows
         return shard
 
@@ -274,19 +301,32 @@ class Decoder:
     # Linears are launched with programmatic dependent launch: their kernels
     # wait on the previous kernel before reading its output, and start
     # streaming weights (which nothing in the step writes) before that.
+    def _workspace_bytes(self, w: QuantWeight, tokens: int) -> int:
+        if w.input_scale is not None:
+            return self.lib.leafq_linear_smooth_workspace_bytes(tokens, w.cols, self.activation_bits)
+        return self.lib.leafq_linear_workspace_bytes(tokens, w.cols, w.bits, w.group, self.activation_bits)
+
     def _linear(self, x: torch.Tensor, w: QuantWeight, out: torch.Tensor, tokens: int,
                 workspace: Workspace) -> None:
+        """Decoder::Impl::linear for one (stacked) weight: input scale, linear,
+        bias (decoder.cpp:994-1233)."""
         lib = self.lib
-        need = lib.leafq_linear_workspace_bytes(tokens, w.cols, w.bits, w.group, self.activation_bits)
+        need = self._workspace_bytes(w, tokens)
         ws = workspace.buffer if need else None
         if ws is not None and ws.numel() < need:
             raise LeafError(_lib.LEAFQ_ERR_INVALID, "decoder workspace too small")
         dst, gather = self._sharded_out(w, out, tokens)
-        check(lib.leafq_linear(_stream(), x.data_ptr(), tokens, w.cols, w.data.data_ptr(),
-                               None if w.scales is None else w.scales.data_ptr(), w.rows, w.bits,
-                               w.group, self.activation_bits, None, dst.data_ptr(),
-                               None if ws is None else ws.data_ptr(), 0 if ws is None else ws.numel(),
-                               LEAFQ_FLAG_PDL))
+        bias = None if w.bias is None else w.bias.data_ptr()
+        scales = None if w.scales is None else w.scales.data_ptr()
+        wsp, wsn = (None, 0) if ws is None else (ws.data_ptr(), ws.numel())
+        if w.input_scale is not None:
+            check(lib.leafq_linear_smooth(_stream(), x.data_ptr(), w.input_scale.data_ptr(), tokens, w.cols,
+                                          w.data.data_ptr(), scales, w.rows, w.bits, w.group, self.activation_bits,
+                                          bias, dst.data_ptr(), wsp, wsn, LEAFQ_FLAG_PDL))
+        else:
+            check(lib.leafq_linear(_stream(), x.data_ptr(), tokens, w.cols, w.data.data_ptr(), scales, w.rows,
+                                   w.bits, w.group, self.activation_bits, bias, dst.data_ptr(), wsp, wsn,
+                                   LEAFQ_FLAG_PDL))
         if gather is not None:
             gather()
 
@@ -306,7 +346,7 @@ class Decoder:
         # before q|k|v and gate|up quantises its output in the same pass
         # (leafq_rmsnorm_quantize), which is what leafq_linear's own
         # quantiser would produce from the fp32 rows.
-        fuse = self.activation_bits == 8 and rows > 8 and c.hidden % 4 == 0 and c.hidden <= 4096
+        fuse = self.activation_bits == 8 and rows > 8 and c.hidden % 4 == 0 and c.hidden <= 4096 and not self.smooth
 
         def norm(delta, add_zero, weight, codes):
             d = None if delta is None else delta.data_ptr()
@@ -323,7 +363,8 @@ class Decoder:
                 dst, gather = self._sharded_out(w, out, rows)
                 check(lib.leafq_linear_int_q(s, b["codes"].data_ptr(), b["code_scales"].data_ptr(), rows, w.cols,
                                              w.data.data_ptr(), w.scales.data_ptr(), w.rows, w.bits, w.group,
-                                             None, dst.data_ptr(), None, LEAFQ_FLAG_PDL))
+                                             None if w.bias is None else w.bias.data_ptr(), dst.data_ptr(), None,
+                                             LEAFQ_FLAG_PDL))
                 if gather is not None:
                     gather()
             else:
@@ -332,7 +373,14 @@ class Decoder:
         norm(None, 0, self.layers[0]["input_norm"], fuse)
         ws = b["attention_ws"]
         for i, layer in enumerate(self.layers):
-            normed_linear(layer["qkv"], b["qkv"])
+            if self.smooth:
+                # Each projection on its own input scale, then q | k | v
+                # side by side in every row as the stacked linear writes them.
+                for n in ("q", "k", "v"):
+                    self._linear(b["normalized"], layer[n], b[n], rows, b["workspace"])
+                torch.cat((b["q"], b["k"], b["v"]), dim=1, out=b["qkv"])
+            else:
+                normed_linear(layer["qkv"], b["qkv"])
             check(lib.leafq_rotary_append_batch(s, b["qkv"].data_ptr(), S, tokens, c.heads, c.kv_heads,
                                                 c.head_dim, c.rotary_dim, self.cos.data_ptr(),
                                                 self.sin.data_ptr(), self.position.data_ptr(),
@@ -345,7 +393,14 @@ class Decoder:
                                             ws.data_ptr(), ws.numel()))
             self._linear(b["attn"], layer["o"], b["o"], rows, b["workspace"])
             norm(b["o"], 0, layer["post_norm"], fuse)
-            normed_linear(layer["gate_up"], b["gate_up"])
+            if self.smooth:
+                # gate and up on their own input scales, interleaved as the
+                # SiLU kernel reads them (gate_0, up_0, gate_1, ...).
+                self._linear(b["normalized"], layer["gate"], b["gate"], rows, b["workspace"])
+                self._linear(b["normalized"], layer["up"], b["up"], rows, b["workspace"])
+                torch.stack((b["gate"], b["up"]), dim=2, out=b["gate_up"].view(rows, c.intermediate, 2))
+            else:
+                normed_linear(layer["gate_up"], b["gate_up"])
             if fuse and c.intermediate <= 6144:
                 # SiLU gate and the down projection's quantisation in one pass.
                 check(lib.leafq_silu_gate_quantize(s, b["gate_up"].data_ptr(), rows, c.intermediate, None,
@@ -354,7 +409,8 @@ class Decoder:
                 dst, gather = self._sharded_out(w, b["down"], rows)
                 check(lib.leafq_linear_int_q(s, b["codes_mlp"].data_ptr(), b["code_scales"].data_ptr(), rows,
                                              w.cols, w.data.data_ptr(), w.scales.data_ptr(), w.rows, w.bits,
-                                             w.group, None, dst.data_ptr(), None, LEAFQ_FLAG_PDL))
+                                             w.group, None if w.bias is None else w.bias.data_ptr(),
+                                             dst.data_ptr(), None, LEAFQ_FLAG_PDL))
                 if gather is not None:
                     gather()
             else:
@@ -526,7 +582,8 @@ class Decoder:
         """The one-launch decode step needs per-row INT8 weights and
         embedding, W8A8, and a cache of at most 4096 rows."""
         per_row = all(w.bits == 8 and w.group == w.cols for w in self._weights())
-        return (per_row and self.sequences == 1 and self.world == 1 and self.activation_bits == 8 and
+        return (per_row and not self.smooth and not self.has_bias and "qkv" in self.layers[0] and
+                self.sequences == 1 and self.world == 1 and self.activation_bits == 8 and
                 self.embed_bits == 8 and
                 self.embed_group == self.cfg.hidden and self.capacity <= 4096 and
                 self.final_norm is not None)

@@ -116,10 +116,19 @@ class OracleDecoder:
         self.length = 0
 
     def _linear(self, x, name):
+        """Decoder::Impl::linear (decoder.cpp:994-1233): the input times the
+        calibrated ``input_scale`` when the artifact has one (:1008-1019, one
+        float multiply per element), the integer linear, then + bias (:1229)."""
         t = self.art.get(name)
+        base = name[:-len(".weight")]
+        scale = self.art.get(base + ".input_scale")
+        bias = self.art.get(base + ".bias")
+        if scale is not None:
+            x = (np.asarray(x, dtype=np.float32) * scale.data.reshape(1, -1)).astype(np.float32)
+        b = None if bias is None else np.ascontiguousarray(bias.data.reshape(-1), dtype=np.float32)
         if self.use_ref:
-            return ref_linear_int(x, t.data, t.scales, t.bits, t.group, None, threads=self.threads)
-        return linear_int(x, t.data, t.scales, t.bits, t.group, None)
+            return ref_linear_int(x, t.data, t.scales, t.bits, t.group, b, threads=self.threads)
+        return linear_int(x, t.data, t.scales, t.bits, t.group, b)
 
     def _rotate(self, x, tokens, nheads, pos):
         c = self.c

@@ -122,11 +122,43 @@ def header_values(shape: LlamaShape):
             0, 0, 0, 1, 0, d, 0, 1, 1.0)
 
 
-def write_artifact(path: Path, shape: LlamaShape, tensors, bits: int = 8, group_size: int = 64):
+def smooth_variant(shape: LlamaShape, tensors, seed: int, biases: bool = True):
+    """The same decoder with the extra tensors the reference decoder looks up
+    for every linear (Decoder::Impl::linear, decoder.cpp:1003-1019): per-column
+    SmoothQuant factors -- each projection's weight columns multiplied by
+    factors f and ``<proj>.input_scale`` = 1 / f (fp32 [1, cols]), as
+    tools/export_decoder.py:383-390 exports a calibrated model -- and, with
+    `biases`, q / k / v projection biases ``<proj>.bias`` (fp32 [1, rows], as
+    a Qwen2 export carries).  Returns (tensors, extras): the modified tensors
+    in tensor order and the extra one-row tensors (name, array)."""
+    rng = np.random.default_rng(seed)
+    smoothed = ("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj", "self_attn.o_proj",
+                "mlp.gate_proj", "mlp.up_proj", "mlp.down_proj")
+    out, extras = [], []
+    for name, array in tensors:
+        base = name[:-len(".weight")] if name.endswith(".weight") else name
+        if name.startswith("model.layers.") and base.split(".", 3)[3] in smoothed:
+            cols = array.shape[1]
+            factors = np.clip(np.exp(rng.standard_normal(cols, dtype=np.float32) * np.float32(0.5)),
+                              np.float32(1e-4), np.float32(1e4)).astype(np.float32)
+            array = (array * factors[None, :]).astype(np.float32)
+            extras.append((base + ".input_scale", (np.float32(1.0) / factors).astype(np.float32)))
+            if biases and base.split(".", 3)[3] in smoothed[:3]:
+                extras.append((base + ".bias", (rng.standard_normal(array.shape[0], dtype=np.float32)
+                                                * np.float32(0.1)).astype(np.float32)))
+        out.append((name, array))
+    return out, extras
+
+
+def write_artifact(path: Path, shape: LlamaShape, tensors, bits: int = 8, group_size: int = 64, extras=()):
     """Write the LEAFDC02 artifact the reference exporter writes for these
     tensors at `bits` (8: per-row INT8; 4: INT4 in groups of min(group_size,
-    cols)).  `tensors` is an iterable of (name, array) in tensor order."""
-    order = shape.tensor_order()
+    cols)).  `tensors` is an iterable of (name, array) in tensor order;
+    `extras` are one-row fp32 tensors (input scales, biases) written after
+    them (the reference decoder finds tensors by name)."""
+    extras = [(name, np.asarray(array, dtype=np.float32).reshape(-1)) for name, array in extras]
+    order = shape.tensor_order() + [(name, 1, array.size) for name, array in extras]
+    tensors = list(tensors) + extras
     descriptors, offset = [], 0
     for name, rows, cols in order:
         precision = bits if rows > 1 else 32

@@ -49,7 +49,13 @@ MODELS = {
     "tiny_w8": (fx.TINY, 2024, 0.1, 11, 24, 32, 8, 64),
     "tiny_w4": (fx.TINY, 2025, 0.1, 12, 24, 32, 4, 32),
     "tinyllama_w8": (fx.TINYLLAMA, 7, 0.0, 3, 128, 128, 8, 64),
+    # SmoothQuant input scales on every projection and q / k / v biases
+    # (fx.smooth_variant).  The reference exporter writes input scales only
+    # from calibration files, so this artifact is written by
+    # decoder_fixture.write_artifact alone and run by the reference decoder.
+    "tiny_smooth": (fx.TINY, 2026, 0.1, 13, 24, 32, 8, 64),
 }
+SMOOTH = {"tiny_smooth"}
 
 
 def sha256(path: Path) -> str:
@@ -83,16 +89,22 @@ def make(name: str) -> None:
     threads = os.cpu_count() or 1
     with tempfile.TemporaryDirectory(dir=os.environ.get("TMPDIR")) as tmp:
         work = Path(tmp)
-        fx.write_snapshot(work / "snapshot", shape, fx.llama_tensors(shape, seed, noise))
-        reference_artifact = work / "reference.leaf"
-        subprocess.run([sys.executable, str(REF / "tools" / "export_decoder.py"), "--model",
-                        str(work / "snapshot"), "--output", str(reference_artifact), "--bits", str(bits),
-                        "--group-size", str(group)], check=True, capture_output=True)
-        mine = work / "mine.leaf"
-        fx.write_artifact(mine, shape, fx.llama_tensors(shape, seed, noise), bits, group)
-        digest = sha256(reference_artifact)
-        if digest != sha256(mine):
-            raise SystemExit(f"{name}: decoder_fixture.write_artifact differs from the reference exporter")
+        if name in SMOOTH:
+            tensors, extras = fx.smooth_variant(shape, fx.llama_tensors(shape, seed, noise), seed + 1)
+            reference_artifact = work / "mine.leaf"
+            fx.write_artifact(reference_artifact, shape, tensors, bits, group, extras=extras)
+            digest = sha256(reference_artifact)
+        else:
+            fx.write_snapshot(work / "snapshot", shape, fx.llama_tensors(shape, seed, noise))
+            reference_artifact = work / "reference.leaf"
+            subprocess.run([sys.executable, str(REF / "tools" / "export_decoder.py"), "--model",
+                            str(work / "snapshot"), "--output", str(reference_artifact), "--bits", str(bits),
+                            "--group-size", str(group)], check=True, capture_output=True)
+            mine = work / "mine.leaf"
+            fx.write_artifact(mine, shape, fx.llama_tensors(shape, seed, noise), bits, group)
+            digest = sha256(reference_artifact)
+            if digest != sha256(mine):
+                raise SystemExit(f"{name}: decoder_fixture.write_artifact differs from the reference exporter")
         ids = fx.prompt_ids(shape, pseed, plen)
         stdout, metrics, _ = run_decoder(reference_artifact, work, "generate", ids, new, threads)
         generated = np.asarray(metrics["generated_tokens"], dtype=np.uint32)

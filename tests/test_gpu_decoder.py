@@ -1,6 +1,8 @@
 """The GPU decoder against the reference decoder (oracle/_ref/leaf_decoder
 outputs recorded by tests/golden/make_decoder_golden.py): identical greedy
-tokens and bit-identical logits (prefill and every decode step).
+tokens and bit-identical logits (prefill and every decode step), for per-row
+INT8, INT4, and an artifact with SmoothQuant input scales on every
+projection and q / k / v biases.
 """
 import hashlib
 import json
@@ -17,8 +19,11 @@ pytestmark = pytest.mark.gpu
 def _artifact(tmp_path, name, shape):
     meta = json.loads((GOLDEN / f"decoder_{name}.json").read_text())
     path = tmp_path / f"{name}.leaf"
-    fx.write_artifact(path, shape, fx.llama_tensors(shape, meta["weight_seed"], meta["norm_noise"]),
-                      meta["bits"], meta["group"])
+    tensors = fx.llama_tensors(shape, meta["weight_seed"], meta["norm_noise"])
+    extras = ()
+    if name == "tiny_smooth":  # SmoothQuant input scales + q / k / v biases
+        tensors, extras = fx.smooth_variant(shape, tensors, meta["weight_seed"] + 1)
+    fx.write_artifact(path, shape, tensors, meta["bits"], meta["group"], extras=extras)
     h = hashlib.sha256()
     with path.open("rb") as f:
         for block in iter(lambda: f.read(1 << 24), b""):
@@ -35,7 +40,7 @@ def _close(got, ref):
     return np.array_equal(got.view(np.uint32), ref.view(np.uint32)), float(np.max(np.abs(got - ref)))
 
 
-@pytest.mark.parametrize("name", ["tiny_w8", "tiny_w4"])
+@pytest.mark.parametrize("name", ["tiny_w8", "tiny_w4", "tiny_smooth"])
 def test_tiny_decoder_matches_reference(cuda_device, tmp_path, name):
     from leaf_b200.decoder import Decoder
 
@@ -152,3 +157,19 @@ def test_expf_matches_libm(cuda_device):
     got = y.cpu().numpy()
     bad = np.flatnonzero(got.view(np.uint32) != expect.view(np.uint32))
     assert bad.size == 0, (x[bad[:5]], got[bad[:5]], expect[bad[:5]])
+
+
+def test_smooth_decoder_batched_prefill_matches_reference(cuda_device, tmp_path):
+    """The SmoothQuant + bias model with several sequences (every linear over
+    all rows, the tcgen05 GEMM for more than 8 rows): each sequence's last
+    prefill logits equal the reference's for its prompt."""
+    from leaf_b200.decoder import Decoder
+
+    path, golden = _artifact(tmp_path, "tiny_smooth", fx.TINY)
+    prompt = golden["prompt"].tolist()
+    dec = Decoder(path, sequences=3)
+    logits = dec.forward_batch([prompt, prompt, prompt]).cpu().numpy()
+    for s in range(3):
+        ok, err = _close(logits[s], golden["prefill_logits"][-1])
+        assert ok, f"sequence {s}: prefill logits differ by {err}"
+    assert dec.device_status() == 0
