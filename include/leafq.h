@@ -148,7 +148,7 @@ int leafq_gemm_i8_per_channel(void* stream, const int8_t* a, const int8_t* b, co
  * int8 [k, n] ([n, k] with trans_b); out fp32 [m, n] =
  * act(alpha * ((float(acc) * input_scale) * weight_scales[col]) + beta * C),
  * C NULL or c_kind 1 (one value), 2 ([n], per column) or 3 ([m, n]);
- * activation 0 none, 1 Relu, 2 Silu (Gelu, 3, returns LEAFQ_ERR_UNSUPPORTED).
+ * activation 0 none, 1 Relu, 2 Silu, 3 Gelu (tanh form, libm tanhf bits).
  * A MatMul node is alpha = 1, beta = 0, C = NULL.  workspace: at least
  * leafq_graph_linear_workspace_bytes(m, k) bytes for the codes; a non-finite
  * input sets *error_flag (device int32, caller clears it). */

@@ -403,11 +403,7 @@ int leafq_graph_linear(void* stream, const float* a, int64_t m, int64_t k, int t
         set_error("unsupported INT8 Gemm C broadcast shape");  // executor.cpp:601-603
         return LEAFQ_ERR_INVALID;
     }
-    if (activation == 3) {
-        set_error("leafq_graph_linear: the fused Gelu (tanhf) is not implemented on the GPU");
-        return LEAFQ_ERR_UNSUPPORTED;
-    }
-    if (activation < 0 || activation > 2) {
+    if (activation < 0 || activation > 3) {
         set_error("leaf::Executor: unsupported fused activation");  // executor.cpp:241
         return LEAFQ_ERR_INVALID;
     }

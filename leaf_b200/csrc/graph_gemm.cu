@@ -31,7 +31,7 @@ struct GraphGlue {
     float alpha, beta;
     const float* c;   // NULL: no C input
     int c_kind;       // 1 scalar, 2 row [n], 3 full [m, n]
-    int activation;   // 0 none, 1 Relu, 2 Silu
+    int activation;   // 0 none, 1 Relu, 2 Silu, 3 Gelu (tanh form)
 };
 
 __device__ __forceinline__ float graph_glue(float value, const GraphGlue& g, int64_t row, int64_t col,
@@ -43,6 +43,7 @@ __device__ __forceinline__ float graph_glue(float value, const GraphGlue& g, int
     }
     if (g.activation == 1) value = value < 0.0f ? 0.0f : value;  // std::max(value, 0.0f)
     if (g.activation == 2) value = __fdiv_rn(value, __fadd_rn(1.0f, expf_libm(-value, tab)));
+    if (g.activation == 3) value = gelu_tanh_libm(value);
     return value;
 }
 

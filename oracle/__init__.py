@@ -72,6 +72,8 @@ def lib() -> ctypes.CDLL:
         _lib.oq_linear_int.argtypes = [_vp, _c_size, _c_size, _vp, _vp, _c_size, ctypes.c_uint,
                                        _c_size, _vp, _vp, _vp, ctypes.c_int]
         _lib.oq_expf.argtypes = [_vp, _vp, _c_size]
+        _lib.oq_gelu.argtypes = [_vp, _vp, _c_size]
+        _lib.oq_tanhf.argtypes = [_vp, _vp, _c_size]
         _lib.oq_linear_float.argtypes = [_vp, _c_size, _c_size, _vp, _vp, _c_size, ctypes.c_uint,
                                          _c_size, _vp, _vp]
         _lib.oq_graph_quantize.argtypes = [_vp, _c_size, ctypes.c_float, _vp]
@@ -103,6 +105,7 @@ def ref() -> ctypes.CDLL:
             getattr(_ref, name).argtypes = [_vp, _vp, _vp, ctypes.c_float, _vp, _vp, _c_size,
                                             _c_size, _c_size, ctypes.c_int]
         _ref.leafref_graph_quantize.argtypes = [_vp, _c_size, ctypes.c_float, _vp]
+        _ref.leafref_graph_activation.argtypes = [_vp, _c_size, ctypes.c_char_p, _vp]
         _ref.leafref_graph_last_error.restype = ctypes.c_char_p
     return _ref
 
@@ -226,6 +229,40 @@ def expf(x):
     return y
 
 
+def gelu(x):
+    """The graph executor's fused Gelu, tanh form (executor.cpp:236-240):
+    (0.5f * v) * (1 + tanhf(c * (v + ((0.044715f * v) * v) * v))), each step
+    one float32 rounding, libm tanhf."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty_like(x)
+    lib().oq_gelu(_p(x), _p(y), x.size)
+    return y
+
+
+def tanhf(x):
+    """libm tanhf elementwise (float32 in, float32 out)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty_like(x)
+    lib().oq_tanhf(_p(x), _p(y), x.size)
+    return y
+
+
+def graph_activation(v, activation):
+    """apply_activation (executor.cpp:232-242): None / "" identity, Relu as
+    std::max(value, 0.0f), Silu v / (1 + expf(-v)), Gelu as gelu()."""
+    f = np.float32
+    v = _f32(v)
+    if activation in (None, ""):
+        return v.copy()
+    if activation == "Relu":
+        return np.where(v < 0, f(0), v).astype(np.float32)
+    if activation == "Silu":
+        return (v / (f(1) + expf(-v))).astype(np.float32)
+    if activation == "Gelu":
+        return gelu(v)
+    raise ValueError(f"leaf::Executor: unsupported fused activation: {activation}")
+
+
 def graph_quantize(x, scale):
     x = _f32(x).reshape(-1)
     q = np.empty(x.shape, dtype=np.int8)
@@ -286,12 +323,7 @@ def graph_linear(a, weight, weight_scales, input_scale, op_type="Gemm", trans_a=
         else:
             raise ValueError("unsupported INT8 Gemm C broadcast shape")
         v = (v + (f(beta) * cb).astype(np.float32)).astype(np.float32)
-    if activation == "Relu":
-        v = np.where(v < 0, f(0), v).astype(np.float32)
-    elif activation == "Silu":
-        v = (v / (f(1) + expf(-v))).astype(np.float32)
-    elif activation not in (None, ""):
-        raise ValueError(f"activation {activation} not restated")
+    v = graph_activation(v, activation)
     return v.reshape(out_shape)
 
 
@@ -357,6 +389,16 @@ def ref_gemm_i8_per_channel(a, b, bias, input_scale, weight_scales, relu=False, 
     fn = ref().leafref_gemm_i8_reference if reference else ref().leafref_gemm_i8_per_channel
     fn(_p(a), _p(b), _p(bias), float(input_scale), _p(weight_scales), _p(out), m, k, n, int(relu))
     return out
+
+
+def ref_graph_activation(x, activation):
+    """The reference's own apply_activation (executor.cpp:232-242) over an
+    array, through oracle/_ref."""
+    x = _f32(x).reshape(-1)
+    y = np.empty_like(x)
+    if ref().leafref_graph_activation(_p(x), x.size, (activation or "").encode(), _p(y)):
+        raise ValueError(ref().leafref_graph_last_error().decode())
+    return y
 
 
 def ref_graph_quantize(x, scale):

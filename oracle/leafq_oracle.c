@@ -208,3 +208,19 @@ void oq_gemm_i8_per_channel(const int8_t* a, const int8_t* b, const float* bias,
 void oq_expf(const float* x, float* y, size_t n) {
     for (size_t i = 0; i < n; ++i) y[i] = expf(x[i]);
 }
+
+/* The graph executor's fused Gelu (executor.cpp:236-240), tanh form, each
+ * step one float rounding in C++'s left-to-right order:
+ * (0.5f * v) * (1 + tanhf(c * (v + ((0.044715f * v) * v) * v))), libm tanhf. */
+void oq_gelu(const float* x, float* y, size_t n) {
+    const float root_two_over_pi = 0.7978845608028654f;
+    for (size_t i = 0; i < n; ++i) {
+        const float v = x[i];
+        y[i] = 0.5f * v * (1.0f + tanhf(root_two_over_pi * (v + 0.044715f * v * v * v)));
+    }
+}
+
+/* y[i] = tanhf(x[i]) (libm). */
+void oq_tanhf(const float* x, float* y, size_t n) {
+    for (size_t i = 0; i < n; ++i) y[i] = tanhf(x[i]);
+}

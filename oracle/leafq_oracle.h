@@ -61,6 +61,13 @@ void oq_gemm_i8_per_channel(const int8_t* a, const int8_t* b, const float* bias,
  * exponential on Linux (transformer.cpp:130, decoder.cpp:983). */
 void oq_expf(const float* x, float* y, size_t n);
 
+/* y[i] = the graph executor's fused Gelu of x[i] (executor.cpp:236-240,
+ * libm tanhf). */
+void oq_gelu(const float* x, float* y, size_t n);
+
+/* y[i] = tanhf(x[i]) (libm). */
+void oq_tanhf(const float* x, float* y, size_t n);
+
 #ifdef __cplusplus
 }
 #endif

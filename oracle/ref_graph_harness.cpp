@@ -1,7 +1,8 @@
 // Test-only harness: appended (on the compiler's stdin) after the reference's
 // unmodified engine/src/executor.cpp so that the graph executor's static INT8
-// activation quantiser (executor.cpp:220-230, anonymous namespace) can be
-// called through a C ABI.  It is the reference oracle for the graph boundary
+// activation quantiser (executor.cpp:220-230) and fused activations
+// (executor.cpp:232-242), both in an anonymous namespace, can be called
+// through a C ABI.  It is the reference oracle for the graph boundary
 // and is never linked into the product.
 
 #include <cstddef>
@@ -23,6 +24,16 @@ int leafref_graph_quantize(const float* values, std::size_t count, float scale, 
     try {
         const auto q = leaf::quantize_input(values, count, scale);
         for (std::size_t i = 0; i < count; ++i) out[i] = q[i];
+        return 0;
+    } catch (const std::exception& e) { graph_harness_error = e.what(); return 1; }
+}
+
+// out[i] = apply_activation(values[i], name): "", "Relu", "Silu" or "Gelu";
+// an unknown name throws (returns 1), as the reference does.
+int leafref_graph_activation(const float* values, std::size_t count, const char* name, float* out) {
+    try {
+        const std::string activation(name);
+        for (std::size_t i = 0; i < count; ++i) out[i] = leaf::apply_activation(values[i], activation);
         return 0;
     } catch (const std::exception& e) { graph_harness_error = e.what(); return 1; }
 }

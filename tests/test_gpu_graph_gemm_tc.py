@@ -5,7 +5,7 @@ leaf::kernels::gemm_i8_per_channel (kernels/gemm.cpp:99-166) and of the
 Gemm / MatMul node (executor.cpp:524-614), bit for bit.  Every shape here
 has row strides that are multiples of 16 bytes, which is what routes it to
 the tensor cores; ragged m / n / k tails, both tile widths (128 and 256
-output columns) and the node glue (C broadcasts, alpha / beta, Relu, Silu)
+output columns) and the node glue (C broadcasts, alpha / beta, Relu, Silu, Gelu)
 are covered."""
 import numpy as np
 import pytest
@@ -53,7 +53,7 @@ def test_gemm_i8_per_channel_extreme_codes(cuda_device):
 
 @pytest.mark.parametrize("trans_a,trans_b", [(0, 0), (1, 0), (0, 1), (1, 1)])
 @pytest.mark.parametrize("c_kind,activation", [(None, None), ("row", "Relu"), ("full", "Silu"),
-                                               ("scalar", None)])
+                                               ("scalar", "Gelu")])
 def test_gemm_node_tensor_cores(cuda_device, trans_a, trans_b, c_kind, activation):
     rng = np.random.default_rng(hash((trans_a, trans_b, c_kind, activation, "tc")) % 2**32)
     m, k, n = 150, 256, 96

@@ -25,7 +25,7 @@ def _case(rng, m, k, n, trans_a, trans_b):
 
 @pytest.mark.parametrize("trans_a,trans_b", [(0, 0), (1, 0), (0, 1), (1, 1)])
 @pytest.mark.parametrize("c_kind", [None, "scalar", "row", "full"])
-@pytest.mark.parametrize("activation", [None, "Relu", "Silu"])
+@pytest.mark.parametrize("activation", [None, "Relu", "Silu", "Gelu"])
 def test_gemm_node_bit_exact(cuda_device, trans_a, trans_b, c_kind, activation):
     rng = np.random.default_rng(hash((trans_a, trans_b, c_kind, activation)) % 2**32)
     m, k, n = 37, 200, 70
@@ -61,11 +61,34 @@ def test_graph_linear_rejections(cuda_device):
         lq.graph_linear(A, W, WS, 0.1, c=torch.zeros(3, device="cuda"))
     with pytest.raises(LeafError, match="activation scale"):
         lq.graph_linear(A, W, WS, 0.0)
-    with pytest.raises(LeafError):
-        lq.graph_linear(A, W, WS, 0.1, activation="Gelu")  # tanhf is not restated
+    with pytest.raises(LeafError, match="unsupported fused activation"):
+        lq.graph_linear(A, W, WS, 0.1, activation="Tanh")
     bad = A.clone()
     bad[1, 3] = float("nan")
     with pytest.raises(LeafError, match="non-finite"):
         lq.graph_linear(bad, W, WS, 0.1)
     with pytest.raises(LeafError, match="transA"):
         lq.graph_linear(A.reshape(2, 2, 32), W, WS, 0.1, trans_a=True)
+
+
+@pytest.mark.parametrize("k,n", [(100, 4141), (256, 4144)])  # CUDA cores (rows not 16-byte) and tensor cores
+def test_gelu_over_sixty_binades(cuda_device, k, n):
+    # Weight scales log-uniform over 1e-30 .. 1e3 put the Gelu's tanhf argument
+    # in every branch of the algorithm (tiny, |x| < 1, |x| >= 1, saturated)
+    # with both signs; the last columns overflow to +-inf before the
+    # activation: Gelu(+inf) = +inf, Gelu(-inf) = -inf * 0 = NaN.  Bits are
+    # compared everywhere except the NaNs' payloads (the x86 default NaN and
+    # the GPU's canonical NaN differ in sign and payload, not in being NaN).
+    rng = np.random.default_rng(k)
+    m = 300
+    a = (rng.standard_normal((m, k)) * 2).astype(np.float32)
+    w = rng.integers(-127, 128, (k, n)).astype(np.int8)
+    ws = np.exp(rng.uniform(np.log(1e-30), np.log(1e3), n)).astype(np.float32)
+    ws[-8:] = np.float32(3e38)
+    expect = oracle.graph_linear(a, w, ws, 0.05, "MatMul", activation="Gelu")
+    got = lq.graph_linear(torch.from_numpy(a).cuda(), torch.from_numpy(w).cuda(), torch.from_numpy(ws).cuda(),
+                          0.05, "MatMul", activation="Gelu").cpu().numpy()
+    nan = np.isnan(expect)
+    assert nan.any() and np.isinf(expect).any()
+    assert np.array_equal(np.isnan(got), nan)
+    assert np.array_equal(got[~nan].view(np.uint32), expect[~nan].view(np.uint32))

@@ -74,3 +74,21 @@ def test_graph_paths():
                               oracle.ref_gemm_i8_per_channel(a, b, bb, 0.0031, scales, relu))
     x = (rng.standard_normal(5000) * 2).astype(np.float32)
     assert np.array_equal(oracle.graph_quantize(x, 0.013), oracle.ref_graph_quantize(x, 0.013))
+
+
+def test_graph_activations():
+    # apply_activation (executor.cpp:232-242) of the reference against the
+    # restatement, over values spanning every float binade, both signs, zeros
+    # and infinities; NaN results compared by position.
+    rng = np.random.default_rng(11)
+    bits = rng.integers(0, 2**32, 400000, dtype=np.uint64).astype(np.uint32)
+    x = bits.view(np.float32)
+    x = np.concatenate([x[np.isfinite(x)], (rng.standard_normal(100000) * 4).astype(np.float32),
+                        np.float32([0.0, -0.0, np.inf, -np.inf, 1e-40, -1e-40, 9.0, -9.0, 22.0, -22.0])])
+    for activation in (None, "Relu", "Silu", "Gelu"):
+        got, ref = oracle.graph_activation(x, activation), oracle.ref_graph_activation(x, activation)
+        nan = np.isnan(ref)
+        assert np.array_equal(np.isnan(got), nan), activation
+        assert np.array_equal(got[~nan].view(np.uint32), ref[~nan].view(np.uint32)), activation
+    with pytest.raises(ValueError, match="unsupported fused activation"):
+        oracle.ref_graph_activation(x[:4], "Tanh")
