@@ -6,6 +6,11 @@
 //   scale = max(absmax / 127, 1e-12) with IEEE division, multiplier =
 //   1 / scale (IEEE), code = round-half-even(x * multiplier).  __fmul_rn and
 //   __fdiv_rn keep the compiler from fusing or approximating any step.
+// quantize_act_warp_kernel: the same arithmetic with one warp per token row
+//   and the row held in registers (rows of at most 2048 aligned floats): one
+//   read of x, a shuffle-only absmax, and up to 16 float4 loads in flight per
+//   lane, where the block kernel reads each row twice across two block
+//   barriers with 2 loads in flight per thread (4096 x 2048: about 2 TB/s).
 // graph_quantize_kernel: the graph executor's static quantiser
 //   (executor.cpp:220-230): division by the calibrated scale, clamp to
 //   [-127, 127], nearbyint.
@@ -91,6 +96,59 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_act_kernel(const float
     }
 }
 
+constexpr int kWarpQuantWarps = 4;  // warps (token rows) per block
+constexpr int kWarpQuantMaxCols = 32 * 4 * 16;
+
+// Token row blockIdx.x * kWarpQuantWarps + warp; lane holds float4 columns lane + 32 j.
+// Requires cols % 4 == 0, x, q and col_scale 16- / 4- / 16-byte aligned (every
+// row too: cols % 4 == 0 keeps x rows 16-byte and code rows 4-byte aligned).
+template <int kVec>
+__global__ void __launch_bounds__(kWarpQuantWarps * 32) quantize_act_warp_kernel(
+    const float* __restrict__ x, int64_t tokens, int64_t cols, int8_t* __restrict__ q, float* __restrict__ scales,
+    const float* __restrict__ col_scale) {
+    grid_dependency_wait();
+    grid_launch_dependents();
+    const int lane = threadIdx.x & 31;
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * kWarpQuantWarps + (threadIdx.x >> 5);
+    if (row >= tokens) return;
+    const int64_t vecs = cols / 4;
+    const float4* in4 = reinterpret_cast<const float4*>(x + row * cols);
+    float4 v[kVec];
+#pragma unroll
+    for (int j = 0; j < kVec; ++j) {
+        const int64_t i = lane + 32 * j;
+        v[j] = i < vecs ? __ldg(in4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float m = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kVec; ++j) {
+        const int64_t i = lane + 32 * j;
+        if (col_scale && i < vecs) v[j] = scale4(v[j], col_scale, i);
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w))));
+    }
+#pragma unroll
+    for (int offset = 16; offset > 0; offset >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, offset));
+    const float scale = fmaxf(__fdiv_rn(m, 127.0f), 1e-12f);
+    const float multiplier = __fdiv_rn(1.0f, scale);
+    if (lane == 0) scales[row] = scale;
+    char4* out4 = reinterpret_cast<char4*>(q + row * cols);
+#pragma unroll
+    for (int j = 0; j < kVec; ++j) {
+        const int64_t i = lane + 32 * j;
+        if (i < vecs)
+            out4[i] = make_char4(code_of(v[j].x, multiplier), code_of(v[j].y, multiplier),
+                                 code_of(v[j].z, multiplier), code_of(v[j].w, multiplier));
+    }
+}
+
+template <int kVec>
+int launch_warp_quant(cudaStream_t s, const float* x, int64_t tokens, int64_t cols, int8_t* q, float* scales,
+                      bool pdl, const float* col_scale) {
+    const int64_t blocks = (tokens + kWarpQuantWarps - 1) / kWarpQuantWarps;
+    return launch(quantize_act_warp_kernel<kVec>, dim3(static_cast<unsigned>(blocks)), dim3(kWarpQuantWarps * 32),
+                  0, s, pdl, "quantize_act_warp", x, tokens, cols, q, scales, col_scale);
+}
+
 __global__ void graph_quantize_kernel(const float* __restrict__ x, int64_t count, float scale,
                                       int8_t* __restrict__ q, int32_t* error_flag) {
     grid_dependency_wait();
@@ -114,6 +172,16 @@ __global__ void graph_quantize_kernel(const float* __restrict__ x, int64_t count
 int launch_quantize_act(cudaStream_t s, const float* x, int64_t tokens, int64_t cols, int8_t* q,
                         float* scales, bool pdl, const float* col_scale) {
     if (tokens == 0) return LEAFQ_OK;
+    const bool warp_rows = cols % 4 == 0 && cols <= kWarpQuantMaxCols && aligned16(x) &&
+                           (reinterpret_cast<uintptr_t>(q) & 3u) == 0 && (!col_scale || aligned16(col_scale));
+    if (warp_rows) {
+        const int64_t vecs = cols / 4;
+        if (vecs <= 32) return launch_warp_quant<1>(s, x, tokens, cols, q, scales, pdl, col_scale);
+        if (vecs <= 64) return launch_warp_quant<2>(s, x, tokens, cols, q, scales, pdl, col_scale);
+        if (vecs <= 128) return launch_warp_quant<4>(s, x, tokens, cols, q, scales, pdl, col_scale);
+        if (vecs <= 256) return launch_warp_quant<8>(s, x, tokens, cols, q, scales, pdl, col_scale);
+        return launch_warp_quant<16>(s, x, tokens, cols, q, scales, pdl, col_scale);
+    }
     return launch(quantize_act_kernel, dim3(static_cast<unsigned>(tokens)), dim3(kQuantThreads), 0,
                   s, pdl, "quantize_act", x, cols, q, scales, col_scale);
 }

@@ -49,9 +49,10 @@ constexpr size_t kYStageBytes = 4 * 32 * 32 * sizeof(float);
 
 // kThin (at most 64 tokens, one M tile): each stage holds only 64 rows of
 // codes, so twice as many stages fit and a whole K of 2048 is in flight at
-// once.  The MMA still reads 128 rows; rows 64..127 fall on the next
-// stage's bytes (or the weight tiles after the last stage) -- in bounds,
-// and their accumulator lanes are never stored.
+// once, and the MMAs are M = 64 (tcgen05.mma kind::i8 128 x N would read
+// past the stage).  The M = 64 accumulator occupies TMEM lanes 0-15 of each
+// 32-lane sub-partition: row 16q + i in lane 32q + i, so epilogue warp q
+// owns rows 16q .. 16q + 15 and stores them through a 16-row TMA box.
 template <int BN, bool kThin>
 struct TileCfg {
     static constexpr int kAStage = kThin ? 64 * BK : kABytes;
@@ -65,8 +66,6 @@ struct TileCfg {
     static constexpr size_t kColBytes = 4 * 2 * 2 * BN * sizeof(float);  // [warp][acc][scale | bias][BN]
     static constexpr size_t kSmemBytes =
         (size_t)kStages * (kAStage + kBBytes) + 1024 /*barriers*/ + kColBytes + kYStageBytes + 1024 /*align*/;
-    static_assert(!kThin || (size_t)kStages * kBBytes >= (size_t)(kABytes - kAStage),
-                  "the last thin stage's unused rows must stay inside the tile region");
 };
 
 struct GemmArgs {
@@ -182,7 +181,7 @@ gemm_w8a8_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
         if (elect_one_sync()) {
-            const uint32_t idesc = umma_idesc_i8(BM, BN);
+            const uint32_t idesc = umma_idesc_i8(kThin ? 64 : BM, BN);
             int it = 0, local = 0;
             bool ok = true;
             for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++local) {
@@ -213,6 +212,7 @@ gemm_w8a8_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
         // ------------------------------------------------ epilogue (warps 2-5)
         grid_dependency_wait();
         const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
+        constexpr int kWarpRows = kThin ? 16 : 32;  // accumulator rows in those lanes
         int local = 0;
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
             const int acc = local & 1;
@@ -231,8 +231,9 @@ gemm_w8a8_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
             __syncwarp();
             if (!mbar_wait(&acc_full[acc], (local >> 1) & 1, kSiteGemmAccFull)) break;
             tcgen05_fence_after();
-            const int64_t m = m0 + quarter * 32 + lane;
-            const bool row_live = m < a.tokens;
+            const int64_t mb = m0 + quarter * kWarpRows;  // this warp's first row
+            const int64_t m = mb + lane;
+            const bool row_live = lane < kWarpRows && m < a.tokens;
             const float token_scale = row_live ? __ldg(a.sx + m) : 0.0f;
             float* out = a.y + m * a.rows;
             const bool vec = (a.rows % 4) == 0;
@@ -255,14 +256,14 @@ gemm_w8a8_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
                     }
                 }
                 if (a.tma_store) {
-                    // This warp's 32 rows x 32 outputs through its staging tile
+                    // This warp's rows x 32 outputs through its staging tile
                     // (rows past the tokens and columns past the rows are not
-                    // written by the store).
+                    // written by the store; with kThin the box is 16 rows and
+                    // lanes 16-31 write nothing).
                     if (lane == 0) bulk_wait_read_all();
                     __syncwarp();
-                    const int64_t mb = m - lane;
                     store_block_32x32(y_stage + quarter * 1024, v, lane, &map_y, static_cast<int32_t>(nb),
-                                      static_cast<int32_t>(mb), nb < a.rows && mb < a.tokens);
+                                      static_cast<int32_t>(mb), nb < a.rows && mb < a.tokens, lane < kWarpRows);
                 } else if (vec && nb + 32 <= a.rows) {
 #pragma unroll
                     for (int j = 0; j < 32; j += 4)
@@ -452,14 +453,12 @@ gemm_w8a8_tc2_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
                     }
                 }
                 if (a.tma_store) {
-                    // This warp's 32 rows x 32 outputs through its staging tile
-                    // (rows past the tokens and columns past the rows are not
-                    // written by the store).
+                    // This warp's 32 rows x 32 outputs through its staging tile.
                     if (lane == 0) bulk_wait_read_all();
                     __syncwarp();
                     const int64_t mb = m - lane;
                     store_block_32x32(y_stage + quarter * 1024, v, lane, &map_y, static_cast<int32_t>(nb),
-                                      static_cast<int32_t>(mb), nb < a.rows && mb < a.tokens);
+                                      static_cast<int32_t>(mb), nb < a.rows && mb < a.tokens, true);
                 } else if (vec && nb + 32 <= a.rows) {
 #pragma unroll
                     for (int j = 0; j < 32; j += 4)
@@ -538,7 +537,7 @@ int make_tma_map_u8(CUtensorMap* map, const void* base, int64_t inner, int64_t o
     return LEAFQ_OK;
 }
 
-int make_tma_map_f32_out(CUtensorMap* map, const void* base, int64_t inner, int64_t outer) {
+int make_tma_map_f32_out(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, int box_rows) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) {
         set_error("cuTensorMapEncodeTiled is not available from the driver");
@@ -546,7 +545,7 @@ int make_tma_map_f32_out(CUtensorMap* map, const void* base, int64_t inner, int6
     }
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(inner) * 4};
-    const cuuint32_t box[2] = {32, 32};
+    const cuuint32_t box[2] = {32, static_cast<cuuint32_t>(box_rows)};
     const cuuint32_t estrides[2] = {1, 1};
     const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box,
                           estrides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -582,7 +581,7 @@ int run_tiles(cudaStream_t s, const int8_t* q, const int8_t* weight, int64_t col
     CUtensorMap map_y = map_q;  // unused unless tma_store
     a.tma_store = rows % 4 == 0 && aligned16(a.y);
     if (a.tma_store) {
-        st = make_tma_map_f32_out(&map_y, a.y, rows, tokens);
+        st = make_tma_map_f32_out(&map_y, a.y, rows, tokens, kThin ? 16 : 32);
         if (st) return st;
     }
     a.n_tiles = static_cast<int>((rows + BN - 1) / BN);
@@ -638,7 +637,7 @@ int run_pairs(cudaStream_t s, const int8_t* q, const int8_t* weight, int64_t col
     CUtensorMap map_y = map_q;  // unused unless tma_store
     a.tma_store = rows % 4 == 0 && aligned16(a.y);
     if (a.tma_store) {
-        st = make_tma_map_f32_out(&map_y, a.y, rows, tokens);
+        st = make_tma_map_f32_out(&map_y, a.y, rows, tokens, 32);
         if (st) return st;
     }
     a.m_tiles = static_cast<int>((tokens + kPairM - 1) / kPairM);

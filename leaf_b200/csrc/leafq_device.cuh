@@ -185,15 +185,19 @@ __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wa
 // 32 values (v), written into a 4 KB shared-memory tile in the 128-byte
 // swizzled layout a TMA store reads (16-byte chunk i of row r at chunk
 // i ^ (r % 8): the lanes of each float4 store hit all 32 banks), then
-// stored by one TMA from lane 0.  The tile's previous store must have
-// finished reading (the caller waits before writing again).
+// stored by one TMA from lane 0.  With a 16-row box (map), only lanes 0-15
+// hold rows and pass `live`.  The tile's previous store must have finished
+// reading (the caller waits before writing again).
 __device__ __forceinline__ void store_block_32x32(float* tile, const float (&v)[32], int lane,
-                                                  const CUtensorMap* map, int32_t c0, int32_t c1, bool issue) {
+                                                  const CUtensorMap* map, int32_t c0, int32_t c1, bool issue,
+                                                  bool live) {
     uint8_t* row = reinterpret_cast<uint8_t*>(tile) + lane * 128;
+    if (live) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
-        *reinterpret_cast<float4*>(row + ((i ^ (lane & 7)) << 4)) =
-            make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        for (int i = 0; i < 8; ++i)
+            *reinterpret_cast<float4*>(row + ((i ^ (lane & 7)) << 4)) =
+                make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    }
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0 && issue) {
@@ -415,9 +419,9 @@ __device__ __forceinline__ void umma_commit_pair(uint64_t* bar, uint16_t cta_mas
 int make_tma_map_u8(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, int box_inner,
                     int box_outer);
 // The same for a row-major fp32 [outer, inner] matrix (inner a multiple of
-// 4), box [32 rows, 32 floats], 128-byte swizzle: the output blocks of
-// store_block_32x32.
-int make_tma_map_f32_out(CUtensorMap* map, const void* base, int64_t inner, int64_t outer);
+// 4), box [box_rows (16 or 32) rows, 32 floats], 128-byte swizzle: the
+// output blocks of store_block_32x32.
+int make_tma_map_f32_out(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, int box_rows);
 
 // Instruction descriptor for kind::i8 with the B operand MN-major (bit 16):
 // B tiles hold rows of N contiguous, as a [k, n] matrix is stored.

@@ -172,7 +172,8 @@ def test_w8a8_prefill_gemm_down_proj(cuda_device):
 
 
 @pytest.mark.parametrize("m,k,n", [(9, 1040, 300), (200, 2064, 257), (129, 128, 513), (640, 512, 256),
-                                   (16, 256, 9500), (64, 2048, 2560), (64, 512, 20000), (40, 256, 38000)])
+                                   (16, 256, 9500), (64, 2048, 2560), (64, 512, 20000), (40, 256, 38000),
+                                   (12, 512, 1001), (33, 528, 4098), (17, 4096, 5000)])
 def test_w8a8_prefill_gemm_ragged(cuda_device, m, k, n):
     """Tiles cut by M, N and K edges (K a multiple of 16 but not of 128), and
     every tile width (on 148 SMs: 32, 64, 128 and 256 rows per tile), with
@@ -186,11 +187,14 @@ def test_w8a8_prefill_gemm_ragged(cuda_device, m, k, n):
     assert bits_equal(y, oracle.linear_int(x, payload, scales, 8, k, bias))
 
 
-def test_tensor_core_accumulators_exact(cuda_device):
+@pytest.mark.parametrize("m", [256, 64, 47, 9])
+def test_tensor_core_accumulators_exact(cuda_device, m):
     """With unit scales and no bias the epilogue returns float(acc) exactly
-    (|acc| < 2^24), so the tcgen05 int32 accumulators are checked directly."""
-    rng = np.random.default_rng(5)
-    m, k, n = 256, 2048, 512
+    (|acc| < 2^24), so the tcgen05 int32 accumulators are checked directly:
+    128-row MMAs, and the 64-row MMAs of launches of at most 64 tokens (every
+    accumulator row of each TMEM sub-partition's 16 lanes)."""
+    rng = np.random.default_rng(5 + m)
+    k, n = 2048, 512
     q = rng.integers(-127, 128, (m, k)).astype(np.int8)
     w = rng.integers(-127, 128, (n, k)).astype(np.int8)
     ones_t = np.ones(m, dtype=np.float32)
@@ -219,7 +223,10 @@ def test_grouped_integer_paths(cuda_device, m, bits, group):
 
 def test_act_quant_large_and_odd(cuda_device):
     rng = np.random.default_rng(9)
-    for m, k in ((512, 2048), (3, 5632), (2, 1), (5, 33)):
+    # Rows of at most 2048 aligned floats take the warp-per-row kernel (every
+    # register width: 64, 1000, 2044, 2048 columns); the others the block one.
+    for m, k in ((512, 2048), (3, 5632), (2, 1), (5, 33), (4096, 2048), (100, 64), (70, 1000), (9, 2044),
+                 (33, 2052)):
         x = activations(rng, m, k)
         q, sx = lq.quantize_act(dev(x))
         eq, esx = oracle.quantize_act(x)
