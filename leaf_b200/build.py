@@ -18,7 +18,7 @@ PACKAGE = Path(__file__).resolve().parent
 CSRC = PACKAGE / "csrc"
 LIBRARY = PACKAGE / "libleafq.so"
 SOURCES = ["act_quant.cu", "gemv_w8a8.cu", "gemv_w4a32.cu", "linear_generic.cu", "gemm_tc.cu",
-           "graph_gemm.cu", "api.cu", "static_scratch.cu", "decode_persistent.cu",
+           "gemm_grouped_tc.cu", "graph_gemm.cu", "api.cu", "static_scratch.cu", "decode_persistent.cu",
            "peer_allgather.cu", "decoder_ops.cu", "decode_model.cu"]
 GENCODE = "arch=compute_100a,code=sm_100a"
 

@@ -114,6 +114,15 @@ int launch_gemm_tc(cudaStream_t s, const int8_t* q, const float* sx, int64_t tok
                    int64_t cols, const int8_t* weight, const float* wscales, int64_t rows,
                    const float* bias, float* y, bool pdl);
 
+// tcgen05 INT8 GEMM for grouped INT8 weights (groups a multiple of 32 codes)
+// with more than 8 tokens; `fused` picks the AVX2 + FMA group accumulation,
+// else the VNNI tile's two roundings.
+bool gemm_grouped_tc_supported(int64_t tokens, int64_t cols, int64_t rows, int bits, int64_t group,
+                               const void* weight, const int8_t* q);
+int launch_gemm_grouped_tc(cudaStream_t s, const int8_t* q, const float* sx, int64_t tokens, int64_t cols,
+                           const int8_t* weight, const float* wscales, int64_t rows, int64_t group,
+                           const float* bias, float* y, bool fused, bool pdl);
+
 // Graph executor kernels.
 int launch_graph_quantize(cudaStream_t s, const float* x, int64_t count, float scale, int8_t* q,
                           int32_t* error_flag);

@@ -2,7 +2,10 @@
 // the exact-order generic weight-only kernel (W4A32 / W8A32 / FP32 with any
 // token count or group).
 //
-// linear_int_q_kernel: one warp per (token, row).  Groups are walked in
+// linear_int_q_kernel: one warp per (token, row) -- few tokens, INT4, groups
+//   that are not multiples of 32, or when the int32 group sums are wanted
+//   (grouped INT8 with more tokens runs on the tensor cores instead,
+//   gemm_grouped_tc.cu).  Groups are walked in
 //   order; each group's int32 sum is exact (dp4a when the group is a
 //   multiple of 4 codes), then result = fma(float(acc) * sx, sw, result)
 //   (decoder.cpp:566-568, GCC-fused), or the two-rounding form of the VNNI
@@ -182,6 +185,11 @@ int launch_linear_int_q(cudaStream_t s, const int8_t* q, const float* sx, int64_
                         int bits, int64_t group, const float* bias, float* y, int32_t* acc,
                         bool fused, bool pdl) {
     if (rows == 0 || tokens == 0) return LEAFQ_OK;
+    // Grouped INT8 with many tokens: the tensor cores (same bits; no int32
+    // group sums are written there, so a caller asking for them stays here).
+    if (!acc && gemm_grouped_tc_supported(tokens, cols, rows, bits, group, weight, q))
+        return launch_gemm_grouped_tc(s, q, sx, tokens, cols, static_cast<const int8_t*>(weight), wscales, rows,
+                                      group, bias, y, fused, pdl);
     return launch(linear_int_q_kernel, dim3(warp_grid(rows * tokens, 256)), dim3(256), 0, s, pdl,
                   "linear_int_q", q, sx, tokens, cols, static_cast<const uint8_t*>(weight),
                   wscales, rows, bits, group, bias, y, acc, fused ? 1 : 0);
