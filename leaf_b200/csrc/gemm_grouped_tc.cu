@@ -8,8 +8,8 @@
 // from result = 0.0f, and stores result + bias[n] (:1229).
 //
 // One CTA per 128-token x 64-row tile (persistent over tiles), 320 threads:
-//   warp 0      TMA producer: 128-byte K stages of codes (16 KB) and weight
-//               rows (8 KB), 128-byte swizzle, as the per-row kernel.
+//   warp 0      TMA producer: 256-byte K stages, each two 128-byte swizzled
+//               boxes of codes (2 x 16 KB) and of weight rows (2 x 8 KB).
 //   warp 1      MMA issuer: tcgen05.mma kind::i8, M = 128, N = 64, K = 32
 //               per instruction.  Each group's K range accumulates into its
 //               own 64-column TMEM slot (a ring of 8 slots, 512 columns), and
@@ -34,7 +34,9 @@ namespace {
 
 constexpr int kGBM = 128;
 constexpr int kGBN = 64;
-constexpr int kGBK = 128;  // bytes of K per stage
+constexpr int kGBox = 128;  // bytes of K per TMA box (the 128-byte swizzle span)
+constexpr int kGBoxes = 2;  // boxes per stage
+constexpr int kGBK = kGBox * kGBoxes;  // bytes of K per stage
 constexpr int kGUmmaK = 32;
 constexpr int kGThreads = 320;
 constexpr int kGEpiWarps = 8;
@@ -42,8 +44,10 @@ constexpr int kGSlots = 8;  // TMEM accumulator slots of kGBN columns
 constexpr int kGTmemCols = kGSlots * kGBN;
 constexpr int kGMaxStages = 8;
 constexpr int kGMaxGroups = 256;  // group scales staged per tile: 64 x groups floats
-constexpr uint32_t kGABytes = kGBM * kGBK;
-constexpr uint32_t kGBBytes = kGBN * kGBK;
+constexpr uint32_t kGABox = kGBM * kGBox;
+constexpr uint32_t kGBBox = kGBN * kGBox;
+constexpr uint32_t kGABytes = kGABox * kGBoxes;
+constexpr uint32_t kGBBytes = kGBBox * kGBoxes;
 constexpr size_t kGYStageBytes = (size_t)kGEpiWarps * 32 * 32 * sizeof(float);
 constexpr int kEpiBar = 1;  // named barrier of the epilogue warps
 
@@ -118,7 +122,9 @@ gemm_w8a8_grouped_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __g
                 const int n0 = (blockIdx.x / a.m_tiles) * kGBN;
                 for (int kb = 0; kb < early; ++kb) {
                     mbar_arrive_expect_tx(&full[kb], kGABytes + kGBBytes);
-                    tma_load_2d(b_tiles + (size_t)kb * kGBBytes, &map_w, kb * kGBK, n0, &full[kb], keep);
+                    for (int h = 0; h < kGBoxes; ++h)
+                        tma_load_2d(b_tiles + (size_t)kb * kGBBytes + h * kGBBox, &map_w, kb * kGBK + h * kGBox, n0,
+                                    &full[kb], keep);
                 }
             }
             grid_dependency_wait();
@@ -130,7 +136,9 @@ gemm_w8a8_grouped_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __g
                 for (int kb = 0; kb < kblocks; ++kb, ++it) {
                     const int s = it % S;
                     if (it < early) {
-                        tma_load_2d(a_tiles + (size_t)s * kGABytes, &map_q, kb * kGBK, m0, &full[s], keep);
+                        for (int h = 0; h < kGBoxes; ++h)
+                            tma_load_2d(a_tiles + (size_t)s * kGABytes + h * kGABox, &map_q, kb * kGBK + h * kGBox, m0,
+                                        &full[s], keep);
                         continue;
                     }
                     if (it >= S && !mbar_wait(&empty[s], ((it / S) - 1) & 1, kSiteGemmEmpty)) {
@@ -138,8 +146,12 @@ gemm_w8a8_grouped_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __g
                         break;
                     }
                     mbar_arrive_expect_tx(&full[s], kGABytes + kGBBytes);
-                    tma_load_2d(a_tiles + (size_t)s * kGABytes, &map_q, kb * kGBK, m0, &full[s], keep);
-                    tma_load_2d(b_tiles + (size_t)s * kGBBytes, &map_w, kb * kGBK, n0, &full[s], keep);
+                    for (int h = 0; h < kGBoxes; ++h) {
+                        tma_load_2d(a_tiles + (size_t)s * kGABytes + h * kGABox, &map_q, kb * kGBK + h * kGBox, m0,
+                                    &full[s], keep);
+                        tma_load_2d(b_tiles + (size_t)s * kGBBytes + h * kGBBox, &map_w, kb * kGBK + h * kGBox, n0,
+                                    &full[s], keep);
+                    }
                 }
             }
             for (int back = 0; back < S && back < it; ++back) {
@@ -163,10 +175,14 @@ gemm_w8a8_grouped_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __g
                         break;
                     }
                     tcgen05_fence_after();
-                    const uint64_t adesc = umma_desc_k_sw128(smem_u32(a_tiles + (size_t)s * kGABytes));
-                    const uint64_t bdesc = umma_desc_k_sw128(smem_u32(b_tiles + (size_t)s * kGBBytes));
 #pragma unroll
                     for (int k = 0; k < kGBK / kGUmmaK; ++k) {
+                        constexpr int kPerBox = kGBox / kGUmmaK;
+                        const int h = k / kPerBox;
+                        const uint64_t adesc =
+                            umma_desc_k_sw128(smem_u32(a_tiles + (size_t)s * kGABytes + h * kGABox)) + 2 * (k % kPerBox);
+                        const uint64_t bdesc =
+                            umma_desc_k_sw128(smem_u32(b_tiles + (size_t)s * kGBBytes + h * kGBBox)) + 2 * (k % kPerBox);
                         const int step = kb * (kGBK / kGUmmaK) + k;
                         if (step >= ksteps) break;  // the last stage's zero-filled tail
                         const int in_group = step % group_steps;
@@ -180,7 +196,7 @@ gemm_w8a8_grouped_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __g
                             tcgen05_fence_after();
                             d_tmem = tmem_base + slot * kGBN;
                         }
-                        umma_i8(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, in_group != 0);
+                        umma_i8(d_tmem, adesc, bdesc, idesc, in_group != 0);
                         if (in_group == group_steps - 1) {
                             umma_commit(&acc_full[gc % kGSlots]);
                             ++gc;
@@ -295,7 +311,7 @@ bool gemm_grouped_tc_supported(int64_t tokens, int64_t cols, int64_t rows, int b
                                const void* weight, const int8_t* q) {
     (void)rows;
     return bits == 8 && tokens > 8 && group < cols && group % kGUmmaK == 0 && cols % group == 0 &&
-           cols >= kGBK && cols / group <= kGMaxGroups && aligned16(weight) && aligned16(q);
+           cols >= kGBox && cols / group <= kGMaxGroups && aligned16(weight) && aligned16(q);
 }
 
 int launch_gemm_grouped_tc(cudaStream_t s, const int8_t* q, const float* sx, int64_t tokens, int64_t cols,
@@ -333,9 +349,9 @@ int launch_gemm_grouped_tc(cudaStream_t s, const int8_t* q, const float* sx, int
     const size_t smem = (size_t)a.bar_offset + 1024 + 1024;
 
     CUtensorMap map_q, map_w, map_y;
-    int st = make_tma_map_u8(&map_q, q, cols, tokens, kGBK, kGBM);
+    int st = make_tma_map_u8(&map_q, q, cols, tokens, kGBox, kGBM);
     if (st) return st;
-    st = make_tma_map_u8(&map_w, weight, cols, rows, kGBK, kGBN);
+    st = make_tma_map_u8(&map_w, weight, cols, rows, kGBox, kGBN);
     if (st) return st;
     map_y = map_q;  // unused unless tma_store
     if (a.tma_store) {
