@@ -72,8 +72,12 @@ def _case_weight(rows, cols, bits, group, device):
 
     gen = torch.Generator(device=device)
     gen.manual_seed(0)
-    if bits == 8:
+    if bits == 8 and group == cols:
         return random_w8_weight(rows, cols, gen, device)
+    if bits == 8:
+        data = torch.randint(-127, 128, (rows, cols), generator=gen, device=device, dtype=torch.int8)
+        scales = torch.rand(rows, cols // group, generator=gen, device=device) * 1e-3 + 1e-4
+        return lq.QuantWeight(data, scales, rows, cols, 8, group)
     rng = np.random.default_rng(0)
     packed = rng.integers(0, 256, (rows, cols // 2), dtype=np.uint8)
     scales = (rng.random((rows, cols // group), dtype=np.float32) * 1e-3 + 1e-4).astype(np.float32)
@@ -88,6 +92,7 @@ CASES = {
     "gemm": (512, 5632, 2048, 8, 2048, 8),      # config 2 prefill GEMM
     "gemm_down": (512, 2048, 5632, 8, 5632, 8),  # config 2 down_proj shape
     "gemm_big": (4096, 5632, 2048, 8, 2048, 8),  # large-M prefill
+    "gemm_grouped": (512, 5632, 2048, 8, 128, 8),  # config 2 shape, grouped INT8 (int8_group_size 128)
     "w4": (1, 11008, 4096, 4, 32, 32),          # config 1 INT4 weight-only GEMV
     "graph_gemm": None,                          # graph INT8 GEMM, [k, n] weight, m=512 k=2048 n=5632
     "decode_small": None,                        # persistent decode kernel, 3-layer stack
@@ -825,6 +830,21 @@ def linear_rates(device, peak_gbs):
         "peak_source": "2 x measured bf16 burst (no INT8 figure measured)",
         "method": "8 distinct [k, n] weights back to back in one CUDA graph (codes given, output allocated per call)"}
     del bl
+    torch.cuda.empty_cache()
+    # Grouped INT8 (int8_group_size 128) at the config-2 shape on the tensor
+    # cores (gemm_w8a8_grouped_tc_kernel), activation quantisation included.
+    group = 128
+    wl = [_case_weight(5632, 2048, 8, group, device) for _ in range(8)]
+    xk = xg[:, :2048].contiguous()
+    yl = [torch.empty(tokens, 5632, device=device) for _ in wl]
+    us = timed([lambda w=w, y=y: lq.linear(xk, w, out=y, workspace=ws, flags=LEAFQ_FLAG_PDL)
+                for w, y in zip(wl, yl)])
+    tops = 2.0 * tokens * 5632 * 2048 / (us * 1e-6) / 1e12
+    out["gemm_grouped_g128_m512_n5632_k2048"] = {
+        "us_per_call": us, "achieved": tops, "unit": "TOP/s", "peak": peak_top, "frac": tops / peak_top,
+        "peak_source": "2 x measured bf16 burst (no INT8 figure measured)",
+        "method": "8 distinct weights back to back in one CUDA graph (activation quantisation included)"}
+    del wl, yl
     torch.cuda.empty_cache()
     return out
 
