@@ -50,6 +50,7 @@ constexpr uint32_t kGABytes = kGABox * kGBoxes;
 constexpr uint32_t kGBBytes = kGBBox * kGBoxes;
 constexpr size_t kGYStageBytes = (size_t)kGEpiWarps * 32 * 32 * sizeof(float);
 constexpr int kEpiBar = 1;  // named barrier of the epilogue warps
+constexpr int kStageGeneric = -1;
 
 struct GroupedArgs {
     const float* sx;
@@ -64,6 +65,56 @@ struct GroupedArgs {
     int tma_store;  // rows % 4 == 0 and y 16-byte aligned
     uint32_t scale_offset, ystage_offset, bar_offset;  // shared-memory layout (bytes from the aligned base)
 };
+
+// One full stage (8 MMAs of K = 32, two 128-byte boxes: descriptors a0/b0 and
+// a1/b1) without branches between the tensor instructions (a branch beside
+// each MMA, as a per-step group test makes, tripled the MMA thread's time per
+// stage).  GS MMAs per group, GS in {1, 2, 4}: 8 / GS groups per stage; each
+// box's accumulator slots are reserved before its first MMA, and each group
+// is committed after its last MMA.
+template <int GS>
+__device__ __forceinline__ bool issue_stage_groups(uint32_t tmem_base, uint64_t a0, uint64_t a1, uint64_t b0,
+                                                   uint64_t b1, uint32_t idesc, uint32_t& gc, uint64_t* acc_full,
+                                                   uint64_t* acc_empty) {
+    constexpr int kPerBox = 4 / GS;  // groups in each 128-byte box
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        // Reserve the box's slots, then issue its MMAs (the other box's slots
+        // may still be in the epilogue's hands).
+#pragma unroll
+        for (int g = 0; g < kPerBox; ++g) {
+            const uint32_t c = gc + h * kPerBox + g;
+            if (c >= kGSlots && !mbar_wait(&acc_empty[c % kGSlots], ((c / kGSlots) - 1) & 1, kSiteGemmAccEmpty))
+                return false;
+        }
+        tcgen05_fence_after();
+        const uint64_t ad = h == 0 ? a0 : a1, bd = h == 0 ? b0 : b1;
+#pragma unroll
+        for (int g = 0; g < kPerBox; ++g) {
+            const uint32_t slot = (gc + h * kPerBox + g) % kGSlots;
+            const uint32_t d = tmem_base + slot * kGBN;
+#pragma unroll
+            for (int j = 0; j < GS; ++j) {
+                const int k = g * GS + j;  // MMA within the box
+                umma_i8(d, ad + 2 * k, bd + 2 * k, idesc, j != 0 ? 1u : 0u);
+            }
+            umma_commit(&acc_full[slot]);
+        }
+    }
+    gc += 2 * kPerBox;
+    return true;
+}
+
+// One full stage inside a group of whole stages; kFirst: the group's first
+// stage (its first MMA starts the accumulator).
+template <bool kFirst>
+__device__ __forceinline__ void issue_stage_whole(uint32_t d, uint64_t a0, uint64_t a1, uint64_t b0, uint64_t b1,
+                                                  uint32_t idesc) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+        umma_i8(d, (k < 4 ? a0 : a1) + 2 * (k % 4), (k < 4 ? b0 : b1) + 2 * (k % 4), idesc,
+                (kFirst && k == 0) ? 0u : 1u);
+}
 
 __global__ void __launch_bounds__(kGThreads, 1)
 gemm_w8a8_grouped_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_w,
@@ -163,6 +214,13 @@ gemm_w8a8_grouped_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __g
         // ------------------------------------------------ MMA issuer
         if (elect_one_sync()) {
             const uint32_t idesc = umma_idesc_i8(kGBM, kGBN);
+            // The full stages' group pattern: 1, 2 or 4 MMAs per group, 0 for
+            // groups of whole stages, else the generic per-step path.
+            constexpr int kSteps = kGBK / kGUmmaK;
+            const int stage_kind = (group_steps == 1 || group_steps == 2 || group_steps == 4) ? group_steps
+                                   : group_steps % kSteps == 0                                 ? 0
+                                                                                                : kStageGeneric;
+            const int stages_per_group = group_steps / kSteps > 0 ? group_steps / kSteps : 1;
             int it = 0;
             uint32_t gc = 0;  // groups started so far (slot = gc % kGSlots)
             bool ok = true;
@@ -175,31 +233,58 @@ gemm_w8a8_grouped_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __g
                         break;
                     }
                     tcgen05_fence_after();
-#pragma unroll
-                    for (int k = 0; k < kGBK / kGUmmaK; ++k) {
-                        constexpr int kPerBox = kGBox / kGUmmaK;
-                        const int h = k / kPerBox;
-                        const uint64_t adesc =
-                            umma_desc_k_sw128(smem_u32(a_tiles + (size_t)s * kGABytes + h * kGABox)) + 2 * (k % kPerBox);
-                        const uint64_t bdesc =
-                            umma_desc_k_sw128(smem_u32(b_tiles + (size_t)s * kGBBytes + h * kGBBox)) + 2 * (k % kPerBox);
-                        const int step = kb * (kGBK / kGUmmaK) + k;
-                        if (step >= ksteps) break;  // the last stage's zero-filled tail
-                        const int in_group = step % group_steps;
-                        if (in_group == 0) {
-                            const uint32_t slot = gc % kGSlots;
-                            if (gc >= kGSlots &&
-                                !mbar_wait(&acc_empty[slot], ((gc / kGSlots) - 1) & 1, kSiteGemmAccEmpty)) {
-                                ok = false;
-                                break;
+                    const uint32_t a_st = smem_u32(a_tiles + (size_t)s * kGABytes);
+                    const uint32_t b_st = smem_u32(b_tiles + (size_t)s * kGBBytes);
+                    const uint64_t a0 = umma_desc_k_sw128(a_st), a1 = umma_desc_k_sw128(a_st + kGABox);
+                    const uint64_t b0 = umma_desc_k_sw128(b_st), b1 = umma_desc_k_sw128(b_st + kGBBox);
+                    if ((kb + 1) * (kGBK / kGUmmaK) <= ksteps && stage_kind != kStageGeneric) {
+                        if (stage_kind == 1) {
+                            ok = issue_stage_groups<1>(tmem_base, a0, a1, b0, b1, idesc, gc, acc_full, acc_empty);
+                        } else if (stage_kind == 2) {
+                            ok = issue_stage_groups<2>(tmem_base, a0, a1, b0, b1, idesc, gc, acc_full, acc_empty);
+                        } else if (stage_kind == 4) {
+                            ok = issue_stage_groups<4>(tmem_base, a0, a1, b0, b1, idesc, gc, acc_full, acc_empty);
+                        } else {  // whole stages per group
+                            const int pos = kb % stages_per_group;
+                            if (pos == 0) {
+                                const uint32_t slot = gc % kGSlots;
+                                if (gc >= kGSlots &&
+                                    !mbar_wait(&acc_empty[slot], ((gc / kGSlots) - 1) & 1, kSiteGemmAccEmpty))
+                                    ok = false;
+                                tcgen05_fence_after();
+                                d_tmem = tmem_base + slot * kGBN;
+                                if (ok) issue_stage_whole<true>(d_tmem, a0, a1, b0, b1, idesc);
+                            } else {
+                                issue_stage_whole<false>(d_tmem, a0, a1, b0, b1, idesc);
                             }
-                            tcgen05_fence_after();
-                            d_tmem = tmem_base + slot * kGBN;
+                            if (ok && pos == stages_per_group - 1) {
+                                umma_commit(&acc_full[gc % kGSlots]);
+                                ++gc;
+                            }
                         }
-                        umma_i8(d_tmem, adesc, bdesc, idesc, in_group != 0);
-                        if (in_group == group_steps - 1) {
-                            umma_commit(&acc_full[gc % kGSlots]);
-                            ++gc;
+                    } else {
+                        // Partial last stage, or a group size outside the patterns above.
+#pragma unroll
+                        for (int k = 0; k < kGBK / kGUmmaK; ++k) {
+                            const int step = kb * (kGBK / kGUmmaK) + k;
+                            if (step >= ksteps) break;  // the last stage's zero-filled tail
+                            const int in_group = step % group_steps;
+                            if (in_group == 0) {
+                                const uint32_t slot = gc % kGSlots;
+                                if (gc >= kGSlots &&
+                                    !mbar_wait(&acc_empty[slot], ((gc / kGSlots) - 1) & 1, kSiteGemmAccEmpty)) {
+                                    ok = false;
+                                    break;
+                                }
+                                tcgen05_fence_after();
+                                d_tmem = tmem_base + slot * kGBN;
+                            }
+                            umma_i8(d_tmem, (k < 4 ? a0 : a1) + 2 * (k % 4), (k < 4 ? b0 : b1) + 2 * (k % 4), idesc,
+                                    in_group != 0);
+                            if (in_group == group_steps - 1) {
+                                umma_commit(&acc_full[gc % kGSlots]);
+                                ++gc;
+                            }
                         }
                     }
                     umma_commit(&empty[s]);
