@@ -96,7 +96,7 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_act_kernel(const float
     }
 }
 
-constexpr int kWarpQuantWarps = 4;  // warps (token rows) per block
+constexpr int kWarpQuantWarps = 1;  // warps (token rows) per block: small blocks fit beside an early-launched GEMM CTA
 constexpr int kWarpQuantMaxCols = 32 * 4 * 16;
 
 // Token row blockIdx.x * kWarpQuantWarps + warp; lane holds float4 columns lane + 32 j.

@@ -41,11 +41,15 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 128;  // bytes (= int8 elements) of K per stage
 constexpr int UMMA_K = 32;
-constexpr int kThreads = 192;
+constexpr int kThreads = 192;      // CTA-pair kernel: producer, MMA, 4 epilogue warps
+constexpr int kEpiWarps = 8;       // one-CTA kernel: two epilogue warps per TMEM sub-partition
+constexpr int kThreadsOne = (2 + kEpiWarps) * 32;
+constexpr int kEpiBar = 1;         // named barrier of the one-CTA kernel's epilogue warps
 constexpr int kABytes = BM * BK;  // 16 KB
 // Output staging: one 32 x 32 fp32 block (4 KB, 128-byte swizzle) per
 // epilogue warp, written to global memory by a TMA store.
 constexpr size_t kYStageBytes = 4 * 32 * 32 * sizeof(float);
+constexpr size_t kYStageBytesOne = kEpiWarps * 32 * 32 * sizeof(float);
 
 // kThin (at most 64 tokens, one M tile): each stage holds only 64 rows of
 // codes, so twice as many stages fit and a whole K of 2048 is in flight at
@@ -57,15 +61,19 @@ template <int BN, bool kThin>
 struct TileCfg {
     static constexpr int kAStage = kThin ? 64 * BK : kABytes;
     static constexpr int kBBytes = BN * BK;
-    // As many 128-byte K stages as fit in ~200 KB of shared memory.
-    static constexpr int kStages = kThin ? (196608 / (kAStage + kBBytes) < 16 ? 196608 / (kAStage + kBBytes) : 16)
-                                         : (BN == 256 ? 4 : BN == 160 ? 5 : BN == 128 ? 6 : BN == 64 ? 8 : 10);
+    // The tile's [scale | bias][BN], rounded to 1 KB: the output staging
+    // blocks behind it must stay 1024-byte aligned for the 128-byte swizzle.
+    static constexpr size_t kColBytes = (2 * BN * sizeof(float) + 1023) / 1024 * 1024;
+    static constexpr size_t kFixed = 1024 /*barriers*/ + kColBytes + kYStageBytesOne + 1024 /*align*/;
+    // The preferred ring depth, cut to what fits in 227 KB beside the rest.
+    static constexpr int kPrefStages =
+        kThin ? 16 : (BN == 256 ? 4 : BN == 160 ? 5 : BN == 128 ? 6 : BN == 64 ? 8 : 10);
+    static constexpr int kFitStages = static_cast<int>((227 * 1024 - kFixed) / (kAStage + kBBytes));
+    static constexpr int kStages = kPrefStages < kFitStages ? kPrefStages : kFitStages;
     static constexpr int kAccCols = BN;  // TMEM columns per accumulator
     // Allocated TMEM columns: a power of two covering both accumulators.
     static constexpr int kTmemCols = 2 * kAccCols <= 64 ? 64 : 2 * kAccCols <= 128 ? 128 : 2 * kAccCols <= 256 ? 256 : 512;
-    static constexpr size_t kColBytes = 4 * 2 * 2 * BN * sizeof(float);  // [warp][acc][scale | bias][BN]
-    static constexpr size_t kSmemBytes =
-        (size_t)kStages * (kAStage + kBBytes) + 1024 /*barriers*/ + kColBytes + kYStageBytes + 1024 /*align*/;
+    static constexpr size_t kSmemBytes = (size_t)kStages * (kAStage + kBBytes) + kFixed;
 };
 
 struct GemmArgs {
@@ -83,7 +91,7 @@ struct GemmArgs {
 };
 
 template <int BN, bool kThin>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreadsOne, 1)
 gemm_w8a8_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_w,
                     const __grid_constant__ CUtensorMap map_y, const GemmArgs a) {
     using Cfg = TileCfg<BN, kThin>;
@@ -103,10 +111,10 @@ gemm_w8a8_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
     uint64_t* acc_full = empty + kStages;
     uint64_t* acc_empty = acc_full + 2;
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acc_empty + 2);
-    // Each tile's row scales and bias, staged per tile by every epilogue
-    // warp for itself (two copies: one per accumulator).
+    // The tile's row scales and bias, staged once per tile by the epilogue
+    // warps together.
     float* col_s = reinterpret_cast<float*>(b_tiles + (size_t)kStages * kBBytes + 1024);
-    float* y_stage = col_s + Cfg::kColBytes / sizeof(float);  // [4 warps][32 x 32], 1024-byte aligned
+    float* y_stage = col_s + Cfg::kColBytes / sizeof(float);  // [8 warps][32 x 32], 1024-byte aligned
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int kblocks = static_cast<int>((a.cols + BK - 1) / BK);
@@ -119,7 +127,7 @@ gemm_w8a8_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&acc_full[i], 1);
-            mbar_init(&acc_empty[i], 4);  // one arrival per epilogue warp
+            mbar_init(&acc_empty[i], kEpiWarps);  // one arrival per epilogue warp
         }
         fence_barrier_init();
         prefetch_tensormap(&map_q);
@@ -209,27 +217,34 @@ gemm_w8a8_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
             }
         }
     } else {
-        // ------------------------------------------------ epilogue (warps 2-5)
+        // ------------------------------------------------ epilogue (warps 2-9)
+        // Warp w reads TMEM lanes 32 (w % 4) .. + 31 and takes the 32-column
+        // blocks c / 32 = part, part + 2, ... (two warps per sub-partition, so
+        // one's arithmetic overlaps the other's loads and stores).
         grid_dependency_wait();
+        const int ew = warp - 2;
         const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
+        const int part = ew >> 2;
         constexpr int kWarpRows = kThin ? 16 : 32;  // accumulator rows in those lanes
         int local = 0;
+        bool ok = true;  // a failed wait leaves the warps on the same barrier sequence
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
             const int acc = local & 1;
             const int m0 = (tile % a.m_tiles) * BM;
             const int n0 = (tile / a.m_tiles) * BN;
             // Stage this tile's row scales and bias (0 without bias: the
-            // epilogue always adds it) while the MMAs run; this warp's own
-            // copy, so no other warp is waited on.
-            float* ws_s = col_s + (quarter * 2 + acc) * 2 * BN;
+            // epilogue always adds it) while the MMAs run, after every
+            // epilogue warp has finished the previous tile.
+            float* ws_s = col_s;
             float* bias_s = ws_s + BN;
-            for (int i = lane; i < BN; i += 32) {
+            bar_sync(kEpiBar, kEpiWarps * 32);
+            for (int i = ew * 32 + lane; i < BN; i += kEpiWarps * 32) {
                 const int64_t n = n0 + i < a.rows ? n0 + i : a.rows - 1;
                 ws_s[i] = __ldg(a.ws + n);
                 bias_s[i] = a.bias ? __ldg(a.bias + n) : 0.0f;
             }
-            __syncwarp();
-            if (!mbar_wait(&acc_full[acc], (local >> 1) & 1, kSiteGemmAccFull)) break;
+            bar_sync(kEpiBar, kEpiWarps * 32);
+            if (ok && !mbar_wait(&acc_full[acc], (local >> 1) & 1, kSiteGemmAccFull)) ok = false;
             tcgen05_fence_after();
             const int64_t mb = m0 + quarter * kWarpRows;  // this warp's first row
             const int64_t m = mb + lane;
@@ -237,7 +252,7 @@ gemm_w8a8_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
             const float token_scale = row_live ? __ldg(a.sx + m) : 0.0f;
             float* out = a.y + m * a.rows;
             const bool vec = (a.rows % 4) == 0;
-            for (int c = 0; c < BN; c += 32) {
+            for (int c = part * 32; c < BN; c += 64) {
                 uint32_t r[32];
                 tmem_ld_32x32b_x32(tmem_base + acc * kAccCols + c + ((uint32_t)(quarter * 32) << 16), r);
                 tmem_wait_ld();
@@ -262,7 +277,7 @@ gemm_w8a8_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
                     // lanes 16-31 write nothing).
                     if (lane == 0) bulk_wait_read_all();
                     __syncwarp();
-                    store_block_32x32(y_stage + quarter * 1024, v, lane, &map_y, static_cast<int32_t>(nb),
+                    store_block_32x32(y_stage + ew * 1024, v, lane, &map_y, static_cast<int32_t>(nb),
                                       static_cast<int32_t>(mb), nb < a.rows && mb < a.tokens, lane < kWarpRows);
                 } else if (vec && nb + 32 <= a.rows) {
 #pragma unroll
@@ -590,7 +605,7 @@ int run_tiles(cudaStream_t s, const int8_t* q, const int8_t* weight, int64_t col
     constexpr size_t smem = TileCfg<BN, kThin>::kSmemBytes;
     st = allow_smem(reinterpret_cast<const void*>(gemm_w8a8_tc_kernel<BN, kThin>), smem, "gemm_w8a8_tc");
     if (st) return st;
-    return launch(gemm_w8a8_tc_kernel<BN, kThin>, dim3(grid), dim3(kThreads), smem, s, pdl, "gemm_w8a8_tc",
+    return launch(gemm_w8a8_tc_kernel<BN, kThin>, dim3(grid), dim3(kThreadsOne), smem, s, pdl, "gemm_w8a8_tc",
                   map_q, map_w, map_y, a);
 }
 
