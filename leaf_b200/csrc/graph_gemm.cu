@@ -122,19 +122,31 @@ __global__ void __launch_bounds__(256) gemm_i8_per_channel_kernel(
 // which the MMA reads MN-major -- each stage holds BN / 128 boxes of
 // [128 rows of k, 128 columns of n] -- or [n, k] (transB), read K-major.
 // Tile D[128 rows of a, BN columns], BN 256 or 128; warp roles as the
-// prefill GEMM (warp 0 TMA, warp 1 TMEM + MMA issue, warps 2-5 epilogue,
-// persistent over tiles, two accumulators).  The int32 sums are exact, and
-// the epilogue is the reference's, element by element.
-constexpr int GBM = 128, GBK = 128, GUMMA_K = 32, GThreads = 192;
+// prefill GEMM (warp 0 TMA, warp 1 TMEM + MMA issue, warps 2-9 epilogue --
+// two per TMEM sub-partition on alternating 32-column blocks -- persistent
+// over tiles, two accumulators).  The int32 sums are exact, and the epilogue
+// is the reference's, element by element; its outputs leave through 32 x 32
+// shared-memory blocks and TMA stores when the output rows are 16-byte
+// aligned.
+constexpr int GBM = 128, GBK = 128, GUMMA_K = 32;
+constexpr int GEpiWarps = 8;
+constexpr int GThreads = (2 + GEpiWarps) * 32;
+constexpr int GEpiBar = 1;  // named barrier of the epilogue warps
 
 template <int BN>
 struct GraphTc {
     static constexpr int kABytes = GBM * GBK;
     static constexpr int kBBytes = BN * GBK;
-    static constexpr int kStages = BN == 256 ? 4 : 6;
     static constexpr int kTmemCols = 2 * BN;
-    static constexpr size_t kColBytes = 4 * 2 * 2 * BN * sizeof(float);  // [warp][acc][scale | bias][BN]
-    static constexpr size_t kSmemBytes = (size_t)kStages * (kABytes + kBBytes) + 1024 + kColBytes + 1024;
+    // The tile's [scale | bias][BN], rounded to 1 KB (the output blocks behind
+    // it stay 1024-byte aligned for the 128-byte swizzle).
+    static constexpr size_t kColBytes = (2 * BN * sizeof(float) + 1023) / 1024 * 1024;
+    static constexpr size_t kYBytes = (size_t)GEpiWarps * 32 * 32 * sizeof(float);
+    static constexpr size_t kFixed = 1024 + kColBytes + kYBytes + 1024;
+    static constexpr int kPrefStages = BN == 256 ? 4 : 6;
+    static constexpr int kFitStages = static_cast<int>((227 * 1024 - kFixed) / (kABytes + kBBytes));
+    static constexpr int kStages = kPrefStages < kFitStages ? kPrefStages : kFitStages;
+    static constexpr size_t kSmemBytes = (size_t)kStages * (kABytes + kBBytes) + kFixed;
 };
 
 struct GraphTcArgs {
@@ -145,13 +157,15 @@ struct GraphTcArgs {
     int relu;
     int64_t m, n, k;
     int m_tiles, n_tiles;
+    int tma_store;  // n % 4 == 0 and a 16-byte aligned output: stores through map_y
     GraphGlue glue;
 };
 
 template <int BN, bool kMnB>
 __global__ void __launch_bounds__(GThreads, 1)
 graph_gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                     const GraphTcArgs g, const __grid_constant__ ExpTable tab_g) {
+                     const __grid_constant__ CUtensorMap map_y, const GraphTcArgs g,
+                     const __grid_constant__ ExpTable tab_g) {
     using Cfg = GraphTc<BN>;
     constexpr int kStages = Cfg::kStages;
     constexpr int kABytes = Cfg::kABytes;
@@ -168,6 +182,7 @@ graph_gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_con
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acc_empty + 2);
     ExpTable* tab = reinterpret_cast<ExpTable*>(tmem_holder + 2);
     float* col_s = reinterpret_cast<float*>(b_tiles + (size_t)kStages * kBBytes + 1024);
+    float* y_stage = col_s + Cfg::kColBytes / sizeof(float);  // [8 warps][32 x 32], 1024-byte aligned
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int kblocks = static_cast<int>((g.k + GBK - 1) / GBK);
@@ -179,7 +194,7 @@ graph_gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_con
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&acc_full[i], 1);
-            mbar_init(&acc_empty[i], 4);
+            mbar_init(&acc_empty[i], GEpiWarps);
         }
         fence_barrier_init();
         prefetch_tensormap(&map_a);
@@ -262,32 +277,37 @@ graph_gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_con
             }
         }
     } else {
-        // ------------------------------------------------ epilogue (warps 2-5)
+        // ------------------------------------------------ epilogue (warps 2-9)
+        const int ew = warp - 2;
         const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31 = rows of a
+        const int part = ew >> 2;      // 32-column blocks part, part + 2, ...
         int local = 0;
+        bool ok = true;  // a failed wait leaves the warps on the same barrier sequence
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
             const int acc = local & 1;
             const int64_t m0 = (int64_t)(tile % g.m_tiles) * GBM;
             const int64_t n0 = (int64_t)(tile / g.m_tiles) * BN;
-            float* ws_s = col_s + (quarter * 2 + acc) * 2 * BN;
+            float* ws_s = col_s;
             float* bias_s = ws_s + BN;
-            for (int i = lane; i < BN; i += 32) {
+            bar_sync(GEpiBar, GEpiWarps * 32);  // every epilogue warp is done with the previous tile
+            for (int i = ew * 32 + lane; i < BN; i += GEpiWarps * 32) {
                 const int64_t n = n0 + i < g.n ? n0 + i : g.n - 1;
                 ws_s[i] = __ldg(g.ws + n);
                 bias_s[i] = g.bias ? __ldg(g.bias + n) : 0.0f;
             }
-            __syncwarp();
-            if (!mbar_wait(&acc_full[acc], (local >> 1) & 1, kSiteGemmAccFull)) break;
+            bar_sync(GEpiBar, GEpiWarps * 32);
+            if (ok && !mbar_wait(&acc_full[acc], (local >> 1) & 1, kSiteGemmAccFull)) ok = false;
             tcgen05_fence_after();
-            const int64_t row = m0 + quarter * 32 + lane;
+            const int64_t mb = m0 + quarter * 32;
+            const int64_t row = mb + lane;
             const bool live = row < g.m;
             float* out = g.out + row * g.n;
-            for (int c = 0; c < BN; c += 32) {
+            for (int c = part * 32; c < BN; c += 64) {
                 uint32_t r[32];
                 tmem_ld_32x32b_x32(tmem_base + acc * BN + c + ((uint32_t)(quarter * 32) << 16), r);
                 tmem_wait_ld();
                 const int64_t nb = n0 + c;
-                if (!live || nb >= g.n) continue;
+                if (!g.tma_store && (!live || nb >= g.n)) continue;
                 float v[32];
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
@@ -296,12 +316,16 @@ graph_gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_con
                                             ws_s[c + j]);
                     if (g.bias) value = __fadd_rn(value, bias_s[c + j]);
                     if (g.relu) value = value < 0.0f ? 0.0f : value;
-                    if (g.glue.on && nb + j < g.n) value = graph_glue(value, g.glue, row, nb + j, g.n, *tab);
+                    if (g.glue.on && live && nb + j < g.n) value = graph_glue(value, g.glue, row, nb + j, g.n, *tab);
                     v[j] = value;
                 }
-                // 32 consecutive outputs of this row: float4 stores when the row
-                // segment is whole and 16-byte aligned.
-                if (nb + 32 <= g.n && ((reinterpret_cast<uintptr_t>(out + nb) & 15u) == 0)) {
+                if (g.tma_store) {
+                    // Rows past m and columns past n are not written by the store.
+                    if (lane == 0) bulk_wait_read_all();
+                    __syncwarp();
+                    store_block_32x32(y_stage + ew * 1024, v, lane, &map_y, static_cast<int32_t>(nb),
+                                      static_cast<int32_t>(mb), nb < g.n && mb < g.m, true);
+                } else if (nb + 32 <= g.n && ((reinterpret_cast<uintptr_t>(out + nb) & 15u) == 0)) {
 #pragma unroll
                     for (int j = 0; j < 32; j += 4)
                         *reinterpret_cast<float4*>(out + nb + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
@@ -315,6 +339,7 @@ graph_gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_con
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[acc]);
         }
+        if (lane == 0) bulk_wait_all();  // this warp's output stores are done
     }
     tcgen05_fence_before();
     __syncthreads();
@@ -339,13 +364,19 @@ int run_graph_tc(cudaStream_t s, const int8_t* a, const int8_t* b, GraphTcArgs g
     st = kMnB ? make_tma_map_u8(&map_b, b, g.n, g.k, 128, GBK) : make_tma_map_u8(&map_b, b, g.k, g.n, GBK, BN);
     if (st) return st;
     g.n_tiles = static_cast<int>((g.n + BN - 1) / BN);
+    CUtensorMap map_y = map_a;  // unused unless tma_store
+    g.tma_store = g.n % 4 == 0 && aligned16(g.out);
+    if (g.tma_store) {
+        st = make_tma_map_f32_out(&map_y, g.out, g.n, g.m, 32);
+        if (st) return st;
+    }
     const int64_t tiles = (int64_t)g.m_tiles * g.n_tiles;
     const int grid = static_cast<int>(std::min<int64_t>(tiles, sm_count()));
     constexpr size_t smem = GraphTc<BN>::kSmemBytes;
     st = allow_smem(reinterpret_cast<const void*>(graph_gemm_tc_kernel<BN, kMnB>), smem, "graph_gemm_tc");
     if (st) return st;
     return launch(graph_gemm_tc_kernel<BN, kMnB>, dim3(grid), dim3(GThreads), smem, s, false, "graph_gemm_tc",
-                  map_a, map_b, g, exp_table());
+                  map_a, map_b, map_y, g, exp_table());
 }
 
 int launch_graph_tc(cudaStream_t s, const int8_t* a, const int8_t* b, int b_kmajor, const float* bias,
