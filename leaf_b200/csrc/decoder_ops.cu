@@ -523,7 +523,27 @@ __global__ void __launch_bounds__(kGroupThreads) attention_group_kernel(
         if (c0 + kGroupRows < keys)
             fetch_rows<DIM>(pre, vbase + (c0 + kGroupRows) * DIM,
                             static_cast<int>(min64(kGroupRows, keys - c0 - kGroupRows)));
-        for (int k = 0; k < n; ++k) {
+        // Four keys per step: each head's four probabilities in one 16-byte
+        // load (c0 and k are multiples of 4, ld too), the additions in key order.
+        int k = 0;
+        for (; k + 4 <= n; k += 4) {
+            const float v0 = rows_s[k * DIM + d], v1 = rows_s[(k + 1) * DIM + d];
+            const float v2 = rows_s[(k + 2) * DIM + d], v3 = rows_s[(k + 3) * DIM + d];
+#pragma unroll
+            for (int j = 0; j < kAcc; ++j) {
+                const int h = h0 + j * kPass;
+                if (h < group) {
+                    const float4 p = *reinterpret_cast<const float4*>(scores + h * ld + c0 + k);
+                    float a = acc[j];
+                    a = __fadd_rn(a, __fmul_rn(p.x, v0));
+                    a = __fadd_rn(a, __fmul_rn(p.y, v1));
+                    a = __fadd_rn(a, __fmul_rn(p.z, v2));
+                    a = __fadd_rn(a, __fmul_rn(p.w, v3));
+                    acc[j] = a;
+                }
+            }
+        }
+        for (; k < n; ++k) {
             const float v = rows_s[k * DIM + d];
 #pragma unroll
             for (int j = 0; j < kAcc; ++j) {
