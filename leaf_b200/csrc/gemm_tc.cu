@@ -59,8 +59,14 @@ constexpr size_t kYStageBytesOne = kEpiWarps * 32 * 32 * sizeof(float);
 // owns rows 16q .. 16q + 15 and stores them through a 16-row TMA box.
 template <int BN, bool kThin>
 struct TileCfg {
-    static constexpr int kAStage = kThin ? 64 * BK : kABytes;
-    static constexpr int kBBytes = BN * BK;
+    // Thin launches take two 128-byte K boxes per stage: half as many stages
+    // (each costs the MMA thread a wait, a commit and a round trip to the
+    // producer), the same bytes in flight.
+    static constexpr int kBoxes = kThin ? 2 : 1;
+    static constexpr int kABox = kThin ? 64 * BK : kABytes;
+    static constexpr int kBBox = BN * BK;
+    static constexpr int kAStage = kABox * kBoxes;
+    static constexpr int kBBytes = kBBox * kBoxes;
     // The tile's [scale | bias][BN], rounded to 1 KB: the output staging
     // blocks behind it must stay 1024-byte aligned for the 128-byte swizzle.
     static constexpr size_t kColBytes = (2 * BN * sizeof(float) + 1023) / 1024 * 1024;
@@ -117,7 +123,9 @@ gemm_w8a8_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
     float* y_stage = col_s + Cfg::kColBytes / sizeof(float);  // [8 warps][32 x 32], 1024-byte aligned
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int kblocks = static_cast<int>((a.cols + BK - 1) / BK);
+    constexpr int kBoxes = Cfg::kBoxes;
+    constexpr int kStageK = BK * kBoxes;  // bytes of K per stage
+    const int kblocks = static_cast<int>((a.cols + kStageK - 1) / kStageK);
     const int tiles = a.m_tiles * a.n_tiles;
 
     if (warp == 0 && lane == 0) {
@@ -154,8 +162,10 @@ gemm_w8a8_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
             {
                 const int n0 = (blockIdx.x / a.m_tiles) * BN;
                 for (int kb = 0; kb < early; ++kb) {
-                    mbar_arrive_expect_tx(&full[kb], a.a_box_bytes + kBBytes);
-                    tma_load_2d(b_tiles + (size_t)kb * kBBytes, &map_w, kb * BK, n0, &full[kb], keep);
+                    mbar_arrive_expect_tx(&full[kb], kBoxes * a.a_box_bytes + kBBytes);
+                    for (int h = 0; h < kBoxes; ++h)
+                        tma_load_2d(b_tiles + (size_t)kb * kBBytes + h * Cfg::kBBox, &map_w, kb * kStageK + h * BK, n0,
+                                    &full[kb], keep);
                 }
             }
             grid_dependency_wait();  // the codes come from the previous kernel
@@ -167,16 +177,22 @@ gemm_w8a8_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
                 for (int kb = 0; kb < kblocks; ++kb, ++it) {
                     const int s = it % kStages;
                     if (it < early) {  // weights already requested
-                        tma_load_2d(a_tiles + (size_t)s * kABytes, &map_q, kb * BK, m0, &full[s], keep);
+                        for (int h = 0; h < kBoxes; ++h)
+                            tma_load_2d(a_tiles + (size_t)s * kABytes + h * Cfg::kABox, &map_q, kb * kStageK + h * BK,
+                                        m0, &full[s], keep);
                         continue;
                     }
                     if (it >= kStages && !mbar_wait(&empty[s], ((it / kStages) - 1) & 1, kSiteGemmEmpty)) {
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&full[s], a.a_box_bytes + kBBytes);
-                    tma_load_2d(a_tiles + (size_t)s * kABytes, &map_q, kb * BK, m0, &full[s], keep);
-                    tma_load_2d(b_tiles + (size_t)s * kBBytes, &map_w, kb * BK, n0, &full[s], keep);
+                    mbar_arrive_expect_tx(&full[s], kBoxes * a.a_box_bytes + kBBytes);
+                    for (int h = 0; h < kBoxes; ++h) {
+                        tma_load_2d(a_tiles + (size_t)s * kABytes + h * Cfg::kABox, &map_q, kb * kStageK + h * BK, m0,
+                                    &full[s], keep);
+                        tma_load_2d(b_tiles + (size_t)s * kBBytes + h * Cfg::kBBox, &map_w, kb * kStageK + h * BK, n0,
+                                    &full[s], keep);
+                    }
                 }
             }
             // Drain: the last use of every stage must have landed before the
@@ -204,12 +220,16 @@ gemm_w8a8_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
                         break;
                     }
                     tcgen05_fence_after();
-                    const uint64_t adesc = umma_desc_k_sw128(smem_u32(a_tiles + (size_t)s * kABytes));
-                    const uint64_t bdesc = umma_desc_k_sw128(smem_u32(b_tiles + (size_t)s * kBBytes));
+                    const uint32_t a_st = smem_u32(a_tiles + (size_t)s * kABytes);
+                    const uint32_t b_st = smem_u32(b_tiles + (size_t)s * kBBytes);
 #pragma unroll
-                    for (int k = 0; k < BK / UMMA_K; ++k) {
-                        // Advance the start address by k * 32 bytes (>> 4).
-                        umma_i8(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
+                    for (int k = 0; k < kBoxes * (BK / UMMA_K); ++k) {
+                        // Box k / 4; advance its start address by (k % 4) * 32 bytes (>> 4).
+                        // Zero-filled steps past the columns add nothing.
+                        constexpr int kPer = BK / UMMA_K;
+                        const uint64_t adesc = umma_desc_k_sw128(a_st + (k / kPer) * Cfg::kABox) + 2 * (k % kPer);
+                        const uint64_t bdesc = umma_desc_k_sw128(b_st + (k / kPer) * Cfg::kBBox) + 2 * (k % kPer);
+                        umma_i8(d_tmem, adesc, bdesc, idesc, (kb | k) != 0);
                     }
                     umma_commit(&empty[s]);
                 }
