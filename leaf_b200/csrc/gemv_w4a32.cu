@@ -271,8 +271,7 @@ __global__ void __launch_bounds__(kThreads32, 1) gemv_w4a32_g32_kernel(const W4A
                 // Loads run 16 groups ahead of the dependent FMAs.
                 float result = 0.0f;
 #pragma unroll 16
-    #pragma unroll 16
-            for (int k = 0; k < G; ++k) result = __fmaf_rn(pr[k], sr[k], result);
+                for (int k = 0; k < G; ++k) result = __fmaf_rn(pr[k], sr[k], result);
                 a.y[r0 + lane] = __fadd_rn(result, bias_r);
             }
             bar_arrive(kBarFree + pb, kParties);

@@ -146,6 +146,26 @@ def test_w4a32_other_groups_and_tokens(cuda_device, m, k, n, group):
     assert bits_equal(y, oracle.linear_float(x, payload, scales, 4, group, bias))
 
 
+@pytest.mark.parametrize("k,n", [(2048, 5632), (8192, 300), (128, 1000), (4096, 33), (1024, 16 * 148 + 5)])
+def test_w4a32_group32_widths(cuda_device, k, n):
+    """The 32-column kernel over 4..256 groups per row (so 128..2 row slots
+    per stage), ragged row counts, every nibble value, a bias, and x with
+    exact zeros, subnormals, tiny and large values."""
+    rng = np.random.default_rng(k * 7 + n)
+    payload = rng.integers(0, 256, size=(n, k // 2), dtype=np.uint8)
+    scales = (rng.random((n, k // 32)) * 1e-2 + 1e-4).astype(np.float32)
+    scales[0, 0] = 3e4
+    x = activations(rng, 1, k)
+    x[0, ::17] = 0.0
+    x[0, 5::97] = np.float32(1.5e-42)
+    x[0, 7::89] = np.float32(-3e-39)
+    x[0, 9::61] *= np.float32(1e25)
+    bias = (rng.standard_normal(n) * 0.01).astype(np.float32)
+    w = lq.QuantWeight.from_host(payload, scales, n, k, 4, 32, bias)
+    y = host(lq.linear(dev(x), w, activation_bits=32))
+    assert bits_equal(y, oracle.linear_float(x, payload, scales, 4, 32, bias))
+
+
 @pytest.mark.parametrize("n", [5632, 2048])
 def test_w8a8_prefill_gemm_config2(cuda_device, n):
     """Config 2: M=512, K=2048, N in {5632, 2048}, 1% x20 outliers; the
