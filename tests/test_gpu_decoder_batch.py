@@ -48,9 +48,27 @@ def _attention(q, kc, vc, start, tokens, heads, kv, scale):
 @pytest.mark.parametrize("heads,kv,dim,tokens", [(8, 2, 64, 1), (8, 2, 64, 5), (32, 4, 64, 40),
                                                  (4, 2, 32, 70), (32, 4, 64, 16), (8, 8, 32, 17)])
 def test_batched_rotary_attention_bit_exact(cuda_device, heads, kv, dim, tokens):
-    rng = np.random.default_rng(heads * 1000 + tokens)
-    S, cap = 3, 192
-    starts = [0, 37, 100]
+    _batched_rotary_attention(heads, kv, dim, tokens, 192, [0, 37, 100], heads * 1000 + tokens)
+
+
+@pytest.mark.parametrize("heads,kv,dim,tokens,cap,starts", [
+    # 20 sequences x 4 kv heads: one block per kv head serving 8 query heads,
+    # caches of 1 to 599 keys across the kernel's staged key and value chunks
+    (32, 4, 64, 1, 600, [0, 62, 63, 64, 126, 127, 128, 129, 254, 255, 256, 383, 384, 447, 510, 511, 512, 513,
+                         575, 598]),
+    (16, 2, 32, 3, 400, [5, 60, 61, 125, 126, 127, 189, 250, 253, 254, 300, 318, 319, 320, 350, 381, 382, 383,
+                         390, 396]),
+    # few blocks: each kv head's query heads split over two blocks
+    (8, 2, 64, 2, 520, [300, 450, 517]),
+    (32, 8, 64, 1, 700, [699, 0, 640]),
+])
+def test_batched_decode_attention_long_caches(cuda_device, heads, kv, dim, tokens, cap, starts):
+    _batched_rotary_attention(heads, kv, dim, tokens, cap, starts, heads * 1000 + tokens + cap)
+
+
+def _batched_rotary_attention(heads, kv, dim, tokens, cap, starts, seed):
+    rng = np.random.default_rng(seed)
+    S = len(starts)
     tables = od.rope_tables(10000.0, dim, cap)
     cos, sin = (torch.from_numpy(t).cuda() for t in tables)
     width = (heads + 2 * kv) * dim
