@@ -172,7 +172,9 @@ __global__ void graph_quantize_kernel(const float* __restrict__ x, int64_t count
 int launch_quantize_act(cudaStream_t s, const float* x, int64_t tokens, int64_t cols, int8_t* q,
                         float* scales, bool pdl, const float* col_scale) {
     if (tokens == 0) return LEAFQ_OK;
-    const bool warp_rows = cols % 4 == 0 && cols <= kWarpQuantMaxCols && aligned16(x) &&
+    // Fewer rows than SMs (decode batches): a 256-thread block per row, so the
+    // row's loads and codes are spread over eight warps instead of one.
+    const bool warp_rows = tokens >= sm_count() && cols % 4 == 0 && cols <= kWarpQuantMaxCols && aligned16(x) &&
                            (reinterpret_cast<uintptr_t>(q) & 3u) == 0 && (!col_scale || aligned16(col_scale));
     if (warp_rows) {
         const int64_t vecs = cols / 4;

@@ -788,6 +788,57 @@ __global__ void __launch_bounds__(kSiluQuantThreads) silu_gate_quantize_kernel(
     }
 }
 
+// Fewer tokens than SMs: a cluster of kSiluCtas CTAs per token, each taking
+// a contiguous quarter of the row; the row's absmax is the maximum of the
+// four CTA maxima, read through distributed shared memory between two
+// cluster barriers (the second keeps every CTA resident until the others
+// have read its maximum).  Values, scale and codes are those of
+// silu_gate_quantize_kernel (the maximum is order-free).
+constexpr int kSiluCtas = 4;
+constexpr int kSiluCtaThreads = 256;
+constexpr int kSiluCtaPer = (kSiluQuantThreads * kSiluQuantPer) / (kSiluCtas * kSiluCtaThreads);  // 6
+
+__global__ void __cluster_dims__(kSiluCtas, 1, 1) __launch_bounds__(kSiluCtaThreads)
+    silu_gate_quantize_cluster_kernel(const float* __restrict__ gate_up, int64_t width, float* __restrict__ act,
+                                      int8_t* __restrict__ codes, float* __restrict__ code_scales,
+                                      const __grid_constant__ ExpTable tab_g) {
+    __shared__ ExpTable tab;
+    if (threadIdx.x < 32) tab.bits[threadIdx.x] = tab_g.bits[threadIdx.x];
+    __shared__ float scratch[33];
+    __syncthreads();
+    const int64_t t = blockIdx.x / kSiluCtas;
+    const uint32_t part = cluster_ctarank();
+    const int64_t c0 = width * part / kSiluCtas, c1 = width * (part + 1) / kSiluCtas;
+    const float2* gu = reinterpret_cast<const float2*>(gate_up) + t * width;
+    float v[kSiluCtaPer];
+    float m = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kSiluCtaPer; ++j) {
+        const int64_t c = c0 + threadIdx.x + (int64_t)j * kSiluCtaThreads;
+        if (c < c1) {
+            const float2 p = __ldg(gu + c);
+            v[j] = silu_gate_one(p.x, p.y, tab);
+            if (act) act[t * width + c] = v[j];
+            m = fmaxf(m, fabsf(v[j]));
+        }
+    }
+    block_max(m, scratch);  // this CTA's maximum in scratch[32]
+    cluster_sync_all();
+    float absmax = 0.0f;
+#pragma unroll
+    for (int r = 0; r < kSiluCtas; ++r)
+        absmax = fmaxf(absmax, ld_shared_cluster_f32(mapa_shared(smem_u32(&scratch[32]), r)));
+    cluster_sync_all();
+    const float scale = fmaxf(__fdiv_rn(absmax, 127.0f), 1e-12f);
+    const float multiplier = __fdiv_rn(1.0f, scale);
+    if (part == 0 && threadIdx.x == 0) code_scales[t] = scale;
+#pragma unroll
+    for (int j = 0; j < kSiluCtaPer; ++j) {
+        const int64_t c = c0 + threadIdx.x + (int64_t)j * kSiluCtaThreads;
+        if (c < c1) codes[t * width + c] = act_code(v[j], multiplier);
+    }
+}
+
 // ----------------------------------------------------------------- argmax
 __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* __restrict__ logits,
                                                                  int64_t width,
@@ -1124,6 +1175,10 @@ int leafq_silu_gate_quantize(void* stream, const float* gate_up, int64_t tokens,
         set_error("leafq_silu_gate_quantize: null pointer");
         return LEAFQ_ERR_INVALID;
     }
+    if (tokens < sm_count())
+        return launch(silu_gate_quantize_cluster_kernel, dim3(static_cast<unsigned>(tokens * kSiluCtas)),
+                      dim3(kSiluCtaThreads), 0, static_cast<cudaStream_t>(stream), false, "silu_gate", gate_up,
+                      width, act, codes, code_scales, exp_table());
     return launch(silu_gate_quantize_kernel, dim3(static_cast<unsigned>(tokens)), dim3(kSiluQuantThreads), 0,
                   static_cast<cudaStream_t>(stream), false, "silu_gate", gate_up, width, act, codes, code_scales,
                   exp_table());

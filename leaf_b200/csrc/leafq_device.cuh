@@ -400,7 +400,15 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t local, uint32_t rank) {
     return r;
 }
 
-// All threads of both CTAs.
+// A float in the shared memory of a CTA of this cluster (shared::cluster
+// address from mapa_shared).
+__device__ __forceinline__ float ld_shared_cluster_f32(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
+
+// All threads of every CTA of the cluster.
 __device__ __forceinline__ void cluster_sync_all() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }

@@ -141,3 +141,26 @@ def test_rotary_attention_silu_bit_exact(cuda_device):
     assert np.array_equal(act2.cpu().numpy().view(np.uint32), expect.view(np.uint32))
     assert np.array_equal(codes.cpu().numpy(), eq)
     assert np.array_equal(sx.cpu().numpy().view(np.uint32), esx.view(np.uint32))
+
+
+@pytest.mark.parametrize("tokens,width", [(64, 5632), (1, 6144), (5, 1001), (2, 3), (150, 5632), (147, 4097)])
+def test_silu_gate_quantize_shapes(cuda_device, tokens, width):
+    """The fused SiLU gate + INT8 quantisation: fewer tokens than SMs take
+    four CTAs per token (row maximum through distributed shared memory), more
+    take one block per token; both against the restatement, bit for bit."""
+    rng = np.random.default_rng(tokens * 7 + width)
+    gu = (rng.standard_normal((tokens, 2 * width)) * 4).astype(np.float32)
+    gu[0, 0:2 * width:7] *= np.float32(30.0)
+    act = torch.empty((tokens, width), device="cuda")
+    codes = torch.empty((tokens, width), dtype=torch.int8, device="cuda")
+    sx = torch.empty(tokens, device="cuda")
+    lib = lq.load()
+    lq._lib.check(lib.leafq_silu_gate_quantize(_s(), torch.from_numpy(gu).cuda().data_ptr(), tokens, width,
+                                               act.data_ptr(), codes.data_ptr(), sx.data_ptr()))
+    g, u = gu[:, 0::2], gu[:, 1::2]
+    expect = u * (g / (np.float32(1) + oracle.expf(-g)))
+    eq, esx = oracle.quantize_act(expect)
+    assert np.array_equal(act.cpu().numpy().view(np.uint32), expect.view(np.uint32))
+    assert np.array_equal(codes.cpu().numpy(), eq)
+    assert np.array_equal(sx.cpu().numpy().view(np.uint32), esx.view(np.uint32))
+    assert lib.leafq_device_status() == 0

@@ -243,10 +243,11 @@ def test_grouped_integer_paths(cuda_device, m, bits, group):
 
 def test_act_quant_large_and_odd(cuda_device):
     rng = np.random.default_rng(9)
-    # Rows of at most 2048 aligned floats take the warp-per-row kernel (every
-    # register width: 64, 1000, 2044, 2048 columns); the others the block one.
+    # At least as many rows as SMs, with at most 2048 aligned floats each: the
+    # warp-per-row kernel (every register width: 64, 200, 500, 1000, 2044, 2048
+    # columns); fewer rows, or other widths: the block-per-row kernel.
     for m, k in ((512, 2048), (3, 5632), (2, 1), (5, 33), (4096, 2048), (100, 64), (70, 1000), (9, 2044),
-                 (33, 2052)):
+                 (33, 2052), (160, 64), (150, 200), (149, 500), (200, 1000), (150, 2044), (147, 2048)):
         x = activations(rng, m, k)
         q, sx = lq.quantize_act(dev(x))
         eq, esx = oracle.quantize_act(x)
