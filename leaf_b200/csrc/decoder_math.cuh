@@ -148,17 +148,20 @@ __device__ __forceinline__ float sum_in_order_par(float4 x, const float* v, int 
     const int i2 = mine & !h2 ? d2 : 0, i3 = mine & !h3 ? d3 : 0;
     const int nh = h0 + h1 + h2 + h3;
     const int incsum = i0 + i1 + i2 + i3;
+    // Within a warp the increments add up to at most 32 x 4 x kElemSat = 2^30: the
+    // warp scan runs in 32 bits, the sums across warps in 64.
     int hinc = nh;
-    long long cinc = incsum;
+    int cinc32 = incsum;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
         const int y = __shfl_up_sync(full, hinc, o);
-        const long long z = __shfl_up_sync(full, cinc, o);
+        const int z = __shfl_up_sync(full, cinc32, o);
         if (lane >= o) {
             hinc += y;
-            cinc += z;
+            cinc32 += z;
         }
     }
+    const long long cinc = cinc32;
     if (lane == 31) {
         ws.warp_heads[warp] = hinc;
         ws.warp_inc[warp] = cinc;
