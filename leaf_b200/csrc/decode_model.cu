@@ -762,14 +762,13 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[b]);
-            // Both rows' sums at once: lanes 0-15 finish with row 2 wi, lanes
-            // 16-31 with row 2 wi + 1 (integer sums: any order).
-            a0 += a0b;
-            a1 += a1b;
+            // Both rows' sums by two independent warp reductions (integer sums:
+            // any order); lanes 0-15 continue with row 2 wi, lanes 16-31 with
+            // row 2 wi + 1.
+            const int sum0 = __reduce_add_sync(0xffffffffu, a0 + a0b);
+            const int sum1 = __reduce_add_sync(0xffffffffu, a1 + a1b);
             const bool hi = lane >= 16;
-            int acc = (hi ? a1 : a0) + __shfl_xor_sync(0xffffffffu, hi ? a0 : a1, 16);
-#pragma unroll
-            for (int o = 8; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+            const int acc = hi ? sum1 : sum0;
             const int64_t row = g.row0 + (int64_t)rb * kRowsPerStage + 2 * wi + (hi ? 1 : 0);
             const int src = (rb / kGroups) & 31;
             const float sw0 = __shfl_sync(0xffffffffu, row_scale.x, src);
