@@ -499,8 +499,7 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
             // The keys are consumed: values into the same region now, while
             // the softmax runs.
             if (tid == 0 && nvchunks > 0 && !side_by_side) issue(vc, vbuf, &att_bar[1], 0);
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) local_max = fmaxf(local_max, __shfl_xor_sync(0xffffffffu, local_max, o));
+            local_max = warp_max_f32(local_max);
             if (lane == 0) partial_max[warp] = local_max;
             consumer_sync();
             float maximum = -INFINITY;
@@ -678,8 +677,7 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
 #pragma unroll
         for (int k = 0; k < kXVec; ++k)
             mx = fmaxf(mx, fmaxf(fmaxf(fabsf(xr[k].x), fabsf(xr[k].y)), fmaxf(fabsf(xr[k].z), fabsf(xr[k].w))));
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        mx = warp_max_f32(mx);
         if (lane == 0) partial_max[warp] = mx;
         consumer_sync();  // also: every warp has finished the previous linear
         if (*abort_flag) return;

@@ -400,6 +400,14 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t local, uint32_t rank) {
     return r;
 }
 
+// Maximum over the full warp (every lane must call it).  Like fmaxf, a NaN
+// operand is dropped in favour of a number.
+__device__ __forceinline__ float warp_max_f32(float v) {
+    float r;
+    asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+    return r;
+}
+
 // A float in the shared memory of a CTA of this cluster (shared::cluster
 // address from mapa_shared).
 __device__ __forceinline__ float ld_shared_cluster_f32(uint32_t addr) {
