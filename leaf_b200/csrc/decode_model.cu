@@ -502,9 +502,8 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
             local_max = warp_max_f32(local_max);
             if (lane == 0) partial_max[warp] = local_max;
             consumer_sync();
-            float maximum = -INFINITY;
-#pragma unroll
-            for (int w = 0; w < kConsumerWarps; ++w) maximum = fmaxf(maximum, partial_max[w]);
+            static_assert(kConsumerWarps <= 32 && (kConsumerWarps & (kConsumerWarps - 1)) == 0, "");
+            const float maximum = warp_max_f32(partial_max[lane & (kConsumerWarps - 1)]);
             for (int64_t k = tid; k < keys; k += kNC) scores[k] = expf_libm(__fsub_rn(scores[k], maximum), *tab_s);
             consumer_sync();
             if (tid == 0) {
@@ -681,9 +680,7 @@ decode_model_kernel(const MOp* __restrict__ ops, int nops, const __grid_constant
         if (lane == 0) partial_max[warp] = mx;
         consumer_sync();  // also: every warp has finished the previous linear
         if (*abort_flag) return;
-        float absmax = 0.0f;
-#pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) absmax = fmaxf(absmax, partial_max[w]);
+        const float absmax = warp_max_f32(partial_max[lane & (kConsumerWarps - 1)]);
         const float xscale = fmaxf(__fdiv_rn(absmax, 127.0f), 1e-12f);
         const float mul = __fdiv_rn(1.0f, xscale);
         char4* out4 = reinterpret_cast<char4*>(codes);
