@@ -167,22 +167,21 @@ __device__ __forceinline__ float sum_in_order_par(float4 x, const float* v, int 
         ws.warp_inc[warp] = cinc;
     }
     sync();
-    int hscan = lane < W ? ws.warp_heads[lane] : 0;
-    long long cscan = lane < W ? ws.warp_inc[lane] : 0;
-#pragma unroll
-    for (int o = 1; o < W; o <<= 1) {
-        const int y = __shfl_up_sync(full, hscan, o);
-        const long long z = __shfl_up_sync(full, cscan, o);
-        if (lane >= o) {
-            hscan += y;
-            cscan += z;
-        }
-    }
-    const int src = warp > 0 ? warp - 1 : 0;
-    const int heads_before = warp > 0 ? __shfl_sync(full, hscan, src) : 0;
-    const long long c_before = warp > 0 ? __shfl_sync(full, cscan, src) : 0;
-    const int heads = __shfl_sync(full, hscan, W - 1);
-    const long long c_total = __shfl_sync(full, cscan, W - 1);
+    // Lane w (< W) holds warp w's heads and increments (at most 2^30, split
+    // into 16-bit limbs so that no 32-bit sum over the block's warps can
+    // wrap); independent warp reductions over the lanes of earlier warps and
+    // over all of them give this warp's offsets and the totals.
+    static_assert(NT / 32 <= 32, "one lane per warp");
+    const bool mine_w = lane < W, earlier = lane < warp;
+    const unsigned hw = mine_w ? static_cast<unsigned>(ws.warp_heads[lane]) : 0u;
+    const unsigned cw = mine_w ? static_cast<unsigned>(ws.warp_inc[lane]) : 0u;
+    const unsigned clo = cw & 0xffffu, chi = cw >> 16;
+    const int heads_before = static_cast<int>(__reduce_add_sync(full, earlier ? hw : 0u));
+    const long long c_before = (static_cast<long long>(__reduce_add_sync(full, earlier ? chi : 0u)) << 16) +
+                               __reduce_add_sync(full, earlier ? clo : 0u);
+    const int heads = static_cast<int>(__reduce_add_sync(full, hw));
+    const long long c_total =
+        (static_cast<long long>(__reduce_add_sync(full, chi)) << 16) + __reduce_add_sync(full, clo);
     if (!fast || heads > OrderedSumScratch<NT>::kPieces) {  // the plain loop
         if (t == 0) {
             float s = 0.0f;
