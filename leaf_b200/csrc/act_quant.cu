@@ -27,15 +27,13 @@ constexpr int kQuantThreads = 256;
 __device__ __forceinline__ int8_t code_of(float value, float multiplier) { return act_code(value, multiplier); }
 
 __device__ __forceinline__ float block_max(float v, float* scratch) {
-    for (int offset = 16; offset > 0; offset >>= 1)
-        v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, offset));
+    v = warp_max_f32(v);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (lane == 0) scratch[warp] = v;
     __syncthreads();
     if (warp == 0) {
         v = lane < (blockDim.x >> 5) ? scratch[lane] : 0.0f;
-        for (int offset = 16; offset > 0; offset >>= 1)
-            v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, offset));
+        v = warp_max_f32(v);
         if (lane == 0) scratch[32] = v;
     }
     __syncthreads();
@@ -126,8 +124,7 @@ __global__ void __launch_bounds__(kWarpQuantWarps * 32) quantize_act_warp_kernel
         if (col_scale && i < vecs) v[j] = scale4(v[j], col_scale, i);
         m = fmaxf(m, fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w))));
     }
-#pragma unroll
-    for (int offset = 16; offset > 0; offset >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, offset));
+    m = warp_max_f32(m);
     const float scale = fmaxf(__fdiv_rn(m, 127.0f), 1e-12f);
     const float multiplier = __fdiv_rn(1.0f, scale);
     if (lane == 0) scales[row] = scale;

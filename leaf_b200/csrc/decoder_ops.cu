@@ -50,14 +50,14 @@ constexpr int kAttnThreads = 128;
 constexpr int kArgmaxThreads = 1024;
 
 __device__ __forceinline__ float block_max(float v, float* scratch) {
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    v = warp_max_f32(v);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     __syncthreads();
     if (lane == 0) scratch[warp] = v;
     __syncthreads();
     if (warp == 0) {
         v = lane < static_cast<int>(blockDim.x >> 5) ? scratch[lane] : -INFINITY;
-        for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+        v = warp_max_f32(v);
         if (lane == 0) scratch[32] = v;
     }
     __syncthreads();
@@ -472,7 +472,7 @@ __global__ void __launch_bounds__(kGroupThreads) attention_group_kernel(
         }
     }
     // ---- per-head maximum (each warp lies within one head: chunk >= 32)
-    for (int o = 16; o > 0; o >>= 1) local_max = fmaxf(local_max, __shfl_xor_sync(0xffffffffu, local_max, o));
+    local_max = warp_max_f32(local_max);
     if ((tid & 31) == 0) red[tid >> 5] = local_max;
     // Start the first value chunk while the softmax runs.
     fetch_rows<DIM>(pre, vbase, static_cast<int>(min64(kGroupRows, keys)));
