@@ -1055,7 +1055,7 @@ def run_batch(args, rank, world, local_rank):
 # dram__bytes_write.sum over decoder_step_bytes, from the ncu capture of
 # `bench.py --case model_small` (3 layers at full width; traffic grows with the
 # weights streamed, each read once, so the ratio carries to the 22-layer step).
-DECODE_TRAFFIC_RATIO = 1.023
+DECODE_TRAFFIC_RATIO = 1.024
 
 
 def main():
