@@ -177,17 +177,15 @@ __global__ void __launch_bounds__(kThreads, 4) gemv_w8a8_kernel(const GemvArgs a
                 }
             }
         }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m[t] = fmaxf(m[t], __shfl_xor_sync(0xffffffffu, m[t], o));
+        m[t] = warp_max_f32(m[t]);
         if (lane == 0) partial_max[warp * MAXT + t] = m[t];
     }
     consumer_sync();
     float multiplier[MAXT];
 #pragma unroll
     for (int t = 0; t < MAXT; ++t) {
-        float absmax = 0.0f;
-#pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) absmax = fmaxf(absmax, partial_max[w * MAXT + t]);
+        static_assert(kConsumerWarps <= 32 && (kConsumerWarps & (kConsumerWarps - 1)) == 0, "");
+        const float absmax = warp_max_f32(partial_max[(lane & (kConsumerWarps - 1)) * MAXT + t]);
         const float scale = fmaxf(__fdiv_rn(absmax, 127.0f), 1e-12f);
         multiplier[t] = __fdiv_rn(1.0f, scale);
         if (tid == 0) token_scale[t] = scale;
