@@ -446,9 +446,12 @@ def run_ours(args, rank, world, local_rank):
     # memory, runs, and copies the produced token back to the host (and
     # waits for it, as a server streaming tokens does).
     # Each step is one replay of Decoder.capture_stream_step's graph (token
-    # in from pinned memory, the fused step, token out to pinned memory).
+    # in from pinned memory, the fused step, token out to pinned memory).  One
+    # pinned word serves as both: the step's result lands where the next step
+    # copies its input from, and the host reads it there after every step.
     tok_in = torch.empty(1, dtype=torch.int32).pin_memory()
-    tok_out = torch.empty(1, dtype=torch.int32).pin_memory()
+    tok_out = tok_in
+    tok_host = tok_out.numpy()
     step_graph = dec.capture_stream_step(tok_in, tok_out)
     first_host = first.cpu()
     for _ in range(3):
@@ -468,7 +471,7 @@ def run_ours(args, rank, world, local_rank):
         for _ in range(r):
             step_graph.replay()
             stream.synchronize()
-            tok_in.copy_(tok_out)
+            streamed = int(tok_host[0])  # the token a server would send now
         done += r
     e_end.record(stream)
     torch.cuda.synchronize(device)

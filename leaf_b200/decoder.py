@@ -622,8 +622,10 @@ class Decoder:
         every token to its client: copy the input token id from pinned host
         memory (``token_in``, int32 [1]), run step_fused(), copy the produced
         token id into pinned host memory (``token_out``).  Replay it, then
-        synchronise the stream before reading ``token_out``.  The graph holds
-        the plan's buffers: delete it before close()."""
+        synchronise the stream before reading ``token_out``.  The two may be
+        the same pinned word: each replay then reads the previous step's token
+        and leaves its own there.  The graph holds the plan's buffers: delete
+        it before close()."""
         if self._plan is None:
             self.build_fused()
         for t in (token_in, token_out):
